@@ -1,0 +1,209 @@
+/*
+ * pace_b200.h — C ABI of the B200 (sm_100a) kernels behind PaceServe's
+ * per-layer custom ops and its KV-transfer path.
+ *
+ * Every entry point takes plain device pointers, element counts and strides,
+ * a dtype code and a cudaStream_t, launches on that stream, never allocates
+ * device memory, never synchronises, and returns a PACE_* status code.  On a
+ * non-zero status, pace_last_error() returns a message for the calling thread.
+ * Row strides are in ELEMENTS of the row's dtype.
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths inside the PaceServe project).
+ */
+#ifndef PACE_B200_H_
+#define PACE_B200_H_
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define PACE_OK 0
+#define PACE_ERR_INVALID_ARGUMENT 1 /* bad shape, stride, null pointer, k > E ... */
+#define PACE_ERR_UNSUPPORTED_DTYPE 2
+#define PACE_ERR_CUDA 3             /* a CUDA runtime call or launch failed     */
+#define PACE_ERR_PEER_ACCESS 4      /* P2P / IPC mapping unavailable            */
+#define PACE_ERR_TOO_LARGE 5        /* a size beyond what the kernel supports   */
+
+/* ---- dtype codes ------------------------------------------------------- */
+#define PACE_F32 0
+#define PACE_F16 1
+#define PACE_BF16 2
+#define PACE_U8 3
+#define PACE_I8 4
+#define PACE_I16 5
+#define PACE_I32 6
+#define PACE_I64 7
+
+/* Message describing the last non-zero status returned on this thread. */
+const char* pace_last_error(void);
+/* Static name of a status code. */
+const char* pace_status_string(int status);
+/* Library version as (major << 16) | (minor << 8) | patch. */
+int pace_version(void);
+/* Programmatic dependent launch (PDL) for the per-layer ops: 1 = on
+ * (default), 0 = plain launches.  Process-wide. */
+void pace_set_pdl(int enable);
+int pace_get_pdl(void);
+
+/* ---- normalisation ------------------------------------------------------
+ * out[t,i] = (T)((T)(x[t,i] * rsqrt(mean_i(x[t,:]^2) + eps)) * w[i]),
+ * fp32 accumulation.  dtype in {F32, F16, BF16}; weight has the same dtype.
+ * Replaces rms_norm (csrc/layernorm.cpp:3-7, csrc/layernorm_kernels.cu:39-62)
+ * called from RMSNorm.forward (paceserve/model_executor/layers/layernorm.py:31-40). */
+int pace_rms_norm(void* out, const void* input, const void* weight, float epsilon,
+                  int64_t num_tokens, int64_t hidden_size, int64_t input_row_stride,
+                  int64_t out_row_stride, int dtype, cudaStream_t stream);
+
+/* In place: residual <- (T)(input + residual); input <- rms_norm(residual).
+ * Replaces the PyTorch add + RMSNorm pair at
+ * paceserve/model_executor/models/llama.py:240-254 (no reference kernel). */
+int pace_fused_add_rms_norm(void* input, void* residual, const void* weight, float epsilon,
+                            int64_t num_tokens, int64_t hidden_size,
+                            int64_t input_row_stride, int64_t residual_row_stride, int dtype,
+                            cudaStream_t stream);
+
+/* ---- rotary embedding ---------------------------------------------------
+ * In place on query [T, num_heads*head_size] and key [T, num_kv_heads*head_size]
+ * (row strides may exceed the row width: q/k views of a fused qkv tensor).
+ * cos_sin_cache is [max_position, rot_dim] = [cos(rot_dim/2) | sin(rot_dim/2)],
+ * of dtype cache_dtype (F32, or the same dtype as q/k).  is_neox: rotate pairs
+ * (i, i + rot_dim/2); otherwise (2i, 2i+1).  Math in fp32.  Tokens whose
+ * position lies outside [0, max_position) are left unchanged.  key may be NULL
+ * when num_kv_heads == 0.
+ * Replaces rotary_embedding (csrc/pos_encoding.cpp:3-9,
+ * csrc/pos_encoding_kernels.cu:80-127) called from RotaryEmbedding.forward
+ * (paceserve/model_executor/layers/rotary_embedding.py:87-103). */
+int pace_rotary_embedding(const int64_t* positions, void* query, void* key, int64_t num_tokens,
+                          int num_heads, int num_kv_heads, int head_size,
+                          int64_t query_row_stride, int64_t key_row_stride,
+                          const void* cos_sin_cache, int cache_dtype, int rot_dim,
+                          int64_t max_position, int is_neox, int dtype, cudaStream_t stream);
+
+/* ---- gated and element-wise activations ---------------------------------
+ * *_and_mul: input [T, 2d] -> out [T, d], out = act(x[:, :d]) * x[:, d:].
+ * Replaces silu_and_mul (csrc/activation.cpp:3-13,
+ * csrc/activation_kernels.cu:29-48) called from SiluAndMul.forward
+ * (paceserve/model_executor/layers/activation.py:19-24) and
+ * paceserve/model_executor/layers/fused_moe/fused_moe.py:518-520.
+ * gelu_and_mul (erf GELU) and gelu_tanh_and_mul have no reference kernel. */
+int pace_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                      int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                      cudaStream_t stream);
+int pace_gelu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                      int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                      cudaStream_t stream);
+int pace_gelu_tanh_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                           int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                           cudaStream_t stream);
+/* Element-wise [T, d] -> [T, d] tanh GELUs with the reference's rounding.
+ * Replace gelu_new / gelu_fast (csrc/activation_kernels.cu:86-114, wrappers
+ * paceserve/model_executor/layers/activation.py:27-43). */
+int pace_gelu_new(void* out, const void* input, int64_t num_tokens, int64_t d,
+                  int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                  cudaStream_t stream);
+int pace_gelu_fast(void* out, const void* input, int64_t num_tokens, int64_t d,
+                   int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                   cudaStream_t stream);
+
+/* ---- MoE routing --------------------------------------------------------
+ * Per row of gating_output [T, E] (fp32): softmax, then top-k by repeated
+ * argmax, ties to the lowest expert index.  topk_weights/topk_indices/
+ * token_expert_indices are [T, k]; token_expert_indices[t, j] = j*T + t.
+ * renormalize != 0 additionally divides each row's k weights by their sum
+ * (the reference does that in Python, fused_moe.py:371-372).  Needs no
+ * workspace for any E.
+ * Replaces topk_softmax (csrc/moe.cpp:3-8, csrc/moe_topk_softmax_kernels.cu:476-503)
+ * called from fused_topk (paceserve/model_executor/layers/fused_moe/fused_moe.py:346-373). */
+int pace_topk_softmax(float* topk_weights, int32_t* topk_indices,
+                      int32_t* token_expert_indices, const float* gating_output,
+                      int64_t num_tokens, int num_experts, int topk, int renormalize,
+                      cudaStream_t stream);
+
+/* Counting sort of the flat topk_ids [numel] (dtype U8/I8/I16/I32/I64) by
+ * expert, each expert's segment padded to a multiple of block_size:
+ *   sorted_token_ids[cumsum[e] + r] = i for the r-th (ascending i) entry of e,
+ *   expert_ids[b] = e for b in [cumsum[e]/bs, cumsum[e+1]/bs),
+ *   *num_tokens_post_pad = cumsum[E].
+ * Slots not written keep their contents (the reference's caller pre-fills them
+ * with numel) unless fill_padding != 0, in which case every padding slot of
+ * sorted_token_ids up to sorted_capacity is set to numel.  Entries whose id is
+ * outside [0, E) are skipped.  sorted_capacity must be >= numel + E*(bs-1),
+ * expert_ids_capacity >= ceil(sorted_capacity / bs).
+ * Replaces moe_align_block_size (csrc/moe.cpp:10-17,
+ * csrc/moe_align_block_size_kernels.cu:112-135) called from
+ * paceserve/model_executor/layers/fused_moe/fused_moe.py:151-204. */
+int pace_moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel,
+                              int num_experts, int block_size, int32_t* sorted_token_ids,
+                              int64_t sorted_capacity, int32_t* expert_ids,
+                              int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
+                              int fill_padding, cudaStream_t stream);
+
+/* ---- paged-KV block transfer --------------------------------------------
+ * A KV cache is one tensor per layer, [num_blocks, 2, block_size, kv_heads,
+ * head_dim], so block b of layer l is the contiguous slab of block_bytes
+ * bytes at layer_ptr[l] + b * block_bytes.
+ *
+ * Copy, for every layer l < num_layers and pair j < num_pairs, the slab
+ * src_block_ids[j] of src_layers[l] onto slab dst_block_ids[j] of dst_layers[l].
+ * src_layers / dst_layers are HOST arrays of num_layers device pointers (each
+ * may be a peer device's memory, reachable after pace_enable_peer_access or
+ * through pace_ipc_open_handle); the two id arrays are DEVICE int32 arrays.
+ * The kernel runs on the stream's device: the destination's device pulls over
+ * NVLink, the source's device pushes.  Pairs with an id outside
+ * [0, src_num_blocks) / [0, dst_num_blocks) are skipped and counted into
+ * *bad_pairs (device int32, may be NULL; the caller zeroes it).  Destination
+ * slabs must not overlap source slabs.  method: 0 = automatic, 1 = SIMT
+ * 16-byte vector copy, 2 = bulk-async (TMA engine) copy staged through shared
+ * memory.  block_bytes must be a multiple of 16 and every layer pointer
+ * 16-byte aligned.
+ * Replaces the GPU->CPU->GPU move of KVhelper.get_kv_cache/insert_kv_cache
+ * (paceserve/kv_transfer/kv_utils.py:33-56) used by BaseWorker._get_kv_cache/
+ * _insert_kv_cache (paceserve/worker/base_worker.py:236-281). */
+int pace_kv_copy_blocks(void* const* src_layers, void* const* dst_layers, int num_layers,
+                        const int32_t* src_block_ids, const int32_t* dst_block_ids,
+                        int64_t num_pairs, int64_t block_bytes, int64_t src_num_blocks,
+                        int64_t dst_num_blocks, int32_t* bad_pairs, int method,
+                        cudaStream_t stream);
+
+/* Gather blocks block_ids[0..n) of every layer into out, laid out
+ * [num_layers, n, block_bytes] contiguous.  out may be device memory or
+ * page-locked host memory mapped into the device (zero-copy).
+ * Replaces KVhelper.get_kv_cache's per-layer fancy-index gather
+ * (paceserve/kv_transfer/kv_utils.py:44-46). */
+int pace_kv_gather_blocks(void* const* layers, int num_layers, const int32_t* block_ids,
+                          int64_t n, int64_t block_bytes, int64_t num_blocks, void* out,
+                          int32_t* bad_ids, cudaStream_t stream);
+
+/* Scatter in = [num_layers, n, block_bytes] onto blocks block_ids[0..n) of every
+ * layer (inverse of pace_kv_gather_blocks).
+ * Replaces KVhelper.insert_kv_cache (paceserve/kv_transfer/kv_utils.py:49-56). */
+int pace_kv_scatter_blocks(const void* in, void* const* layers, int num_layers,
+                           const int32_t* block_ids, int64_t n, int64_t block_bytes,
+                           int64_t num_blocks, int32_t* bad_ids, cudaStream_t stream);
+
+/* ---- peer access and CUDA IPC (KV promotion across processes) ----------- */
+#define PACE_IPC_HANDLE_BYTES 64
+/* Make `peer`'s memory addressable from `device` (idempotent).  New: the
+ * reference moves KV through the Ray object store instead. */
+int pace_enable_peer_access(int device, int peer);
+/* *can = 1 if `device` can address `peer`'s memory directly. */
+int pace_can_access_peer(int device, int peer, int* can);
+/* Export the allocation holding dev_ptr: writes PACE_IPC_HANDLE_BYTES bytes to
+ * handle_out and the byte offset of dev_ptr inside that allocation. */
+int pace_ipc_get_handle(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+/* Map an exported allocation into this process on `device`; *base_out is the
+ * allocation's base (add the exporter's offset). */
+int pace_ipc_open_handle(const void* handle, int device, void** base_out);
+/* Unmap a base returned by pace_ipc_open_handle. */
+int pace_ipc_close_handle(void* base);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PACE_B200_H_ */

@@ -1,0 +1,233 @@
+// Gated activations (silu/gelu/gelu-tanh and mul) and the element-wise tanh
+// GELUs (gelu_new, gelu_fast) for sm_100a.
+//
+// Semantics:
+//  * silu_and_mul: out = (T)((T)silu(x) * y), silu in fp32
+//    (reference csrc/activation_kernels.cu:8-25: silu returns T, the multiply
+//    is a T*T operation, i.e. fp32 multiply then rounding to T).
+//  * gelu_and_mul / gelu_tanh_and_mul: same rounding points, with the erf GELU
+//    and the tanh-approximated GELU (no reference kernel; they match the
+//    PyTorch composition F.gelu(x[:, :d], approximate=...) * x[:, d:]).
+//  * gelu_new / gelu_fast: the reference's formulas with every intermediate
+//    rounded where the reference's T-typed arithmetic rounds
+//    (csrc/activation_kernels.cu:86-98).
+//
+// Design: pure streaming.  2-D grid (row, column chunk), each thread moves U
+// 16-byte vectors per input half with all loads issued before any math, so a
+// CTA keeps 256 * U * 32 bytes in flight.  Unaligned shapes use a scalar
+// kernel with the same arithmetic.
+#include "common.cuh"
+
+namespace pace {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float R(float v) {
+  return Traits<T>::round(v);
+}
+
+struct SiluOp {
+  template <typename T>
+  __device__ __forceinline__ static float act(float x) {
+    return R<T>(x / (1.0f + expf(-x)));
+  }
+};
+
+struct GeluErfOp {
+  template <typename T>
+  __device__ __forceinline__ static float act(float x) {
+    return R<T>(0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)));
+  }
+};
+
+struct GeluTanhOp {
+  template <typename T>
+  __device__ __forceinline__ static float act(float x) {
+    // sqrt(2/pi) and the cubic coefficient of the tanh approximation.
+    const float kBeta = 0.79788456080286535588f;
+    const float kKappa = 0.044715f;
+    const float x3 = x * x * x;
+    const float inner = kBeta * (x + kKappa * x3);
+    return R<T>(0.5f * x * (1.0f + tanhf(inner)));
+  }
+};
+
+// gelu_new with the reference's T-typed intermediate roundings
+// (csrc/activation_kernels.cu:86-91).
+struct GeluNewOp {
+  template <typename T>
+  __device__ __forceinline__ static float act(float x) {
+    const float x3 = R<T>(R<T>(x * x) * x);
+    const float a = R<T>(0.044715f * x3);
+    const float b = R<T>(x + a);
+    const float c = R<T>(0.79788456f * b);
+    const float t = R<T>(tanhf(c));
+    return R<T>(R<T>(0.5f * x) * R<T>(1.0f + t));
+  }
+};
+
+// gelu_fast (csrc/activation_kernels.cu:93-98).
+struct GeluFastOp {
+  template <typename T>
+  __device__ __forceinline__ static float act(float x) {
+    const float a = R<T>(x * 0.79788456f);
+    const float b = R<T>(0.044715f * x);
+    const float d = R<T>(1.0f + R<T>(b * x));
+    const float t = R<T>(tanhf(R<T>(a * d)));
+    return R<T>(R<T>(0.5f * x) * R<T>(1.0f + t));
+  }
+};
+
+// GATED: in row = [x (d) | y (d)], out = act(x) * y.  Otherwise out = act(x).
+template <typename T, typename Op, int U, bool GATED>
+__global__ void __launch_bounds__(256)
+    act_vec_kernel(T* __restrict__ out, const T* __restrict__ in, int64_t d, int64_t in_stride,
+                   int64_t out_stride) {
+  using Tr = Traits<T>;
+  constexpr int V = Tr::kVec;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const int64_t nvec = d / V;
+  const int64_t base = (int64_t)blockIdx.y * (blockDim.x * U) + threadIdx.x;
+  const T* xr = in + row * in_stride;
+  T* orow = out + row * out_stride;
+  uint4 xv[U], yv[U];
+#pragma unroll
+  for (int j = 0; j < U; ++j) {
+    const int64_t c = base + (int64_t)j * blockDim.x;
+    if (c < nvec) {
+      xv[j] = ld_nc_v4(xr + c * V);
+      if (GATED) yv[j] = ld_nc_v4(xr + d + c * V);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < U; ++j) {
+    const int64_t c = base + (int64_t)j * blockDim.x;
+    if (c < nvec) {
+      float x[V], o[V];
+      Tr::unpack(xv[j], x);
+      if (GATED) {
+        float y[V];
+        Tr::unpack(yv[j], y);
+#pragma unroll
+        for (int e = 0; e < V; ++e) o[e] = Op::template act<T>(x[e]) * y[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) o[e] = Op::template act<T>(x[e]);
+      }
+      st_v4(orow + c * V, Tr::pack(o));
+    }
+  }
+}
+
+template <typename T, typename Op, bool GATED>
+__global__ void __launch_bounds__(256)
+    act_scalar_kernel(T* __restrict__ out, const T* __restrict__ in, int64_t d, int64_t in_stride,
+                      int64_t out_stride) {
+  using Tr = Traits<T>;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const T* xr = in + row * in_stride;
+  T* orow = out + row * out_stride;
+  for (int64_t i = (int64_t)blockIdx.y * blockDim.x + threadIdx.x; i < d;
+       i += (int64_t)gridDim.y * blockDim.x) {
+    const float x = Tr::to_f(xr[i]);
+    float o = Op::template act<T>(x);
+    if (GATED) o = o * Tr::to_f(xr[d + i]);
+    orow[i] = Tr::from_f(o);
+  }
+}
+
+template <typename T, typename Op, bool GATED>
+int launch_act(void* out, const void* in, int64_t num_tokens, int64_t d, int64_t in_stride,
+               int64_t out_stride, cudaStream_t stream, const char* name) {
+  constexpr int V = Traits<T>::kVec;
+  T* o = static_cast<T*>(out);
+  const T* x = static_cast<const T*>(in);
+  const bool vec = (d % V == 0) && (in_stride % V == 0) && (out_stride % V == 0) &&
+                   aligned16(out) && aligned16(in);
+  cudaError_t err;
+  if (vec) {
+    const int64_t nvec = d / V;
+    const int dev_sms = sm_count(StreamDeviceGuard(stream).device());
+    // 4 vectors per thread when that still gives every SM two CTAs, else 1.
+    const int64_t ctas4 = ceil_div(nvec, 256 * 4) * num_tokens;
+    if (ctas4 >= 2 * dev_sms) {
+      const dim3 grid((unsigned)num_tokens, (unsigned)ceil_div(nvec, 256 * 4));
+      err = launch(act_vec_kernel<T, Op, 4, GATED>, grid, dim3(256), 0, stream, o, x, d,
+                   in_stride, out_stride);
+    } else {
+      const dim3 grid((unsigned)num_tokens, (unsigned)ceil_div(nvec, 256));
+      err = launch(act_vec_kernel<T, Op, 1, GATED>, grid, dim3(256), 0, stream, o, x, d,
+                   in_stride, out_stride);
+    }
+  } else {
+    const int64_t bx = ceil_div(d, 256) < 64 ? ceil_div(d, 256) : 64;
+    const dim3 grid((unsigned)num_tokens, (unsigned)bx);
+    err = launch(act_scalar_kernel<T, Op, GATED>, grid, dim3(256), 0, stream, o, x, d, in_stride,
+                 out_stride);
+  }
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  return PACE_OK;
+}
+
+template <typename Op, bool GATED>
+int act_entry(void* out, const void* input, int64_t num_tokens, int64_t d, int64_t in_stride,
+              int64_t out_stride, int dtype, cudaStream_t stream, const char* name) {
+  if (num_tokens < 0 || d < 0 || num_tokens > INT32_MAX)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad shape [%lld, %lld]", name,
+                (long long)num_tokens, (long long)d);
+  if (d / 8 > 65535LL * 256)
+    return fail(PACE_ERR_TOO_LARGE, "%s: row width %lld too large", name, (long long)d);
+  const int64_t in_w = GATED ? 2 * d : d;
+  if (in_stride < in_w || out_stride < d)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: row stride smaller than the row", name);
+  if (num_tokens == 0 || d == 0) return PACE_OK;
+  if (!out || !input) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  StreamDeviceGuard guard(stream);
+  return PACE_DISPATCH_FLOAT(dtype, name, [&] {
+    return launch_act<scalar_t, Op, GATED>(out, input, num_tokens, d, in_stride, out_stride,
+                                           stream, name);
+  });
+}
+
+}  // namespace
+}  // namespace pace
+
+extern "C" int pace_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                                 int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                                 cudaStream_t stream) {
+  return pace::act_entry<pace::SiluOp, true>(out, input, num_tokens, d, input_row_stride,
+                                             out_row_stride, dtype, stream, "silu_and_mul");
+}
+
+extern "C" int pace_gelu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                                 int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                                 cudaStream_t stream) {
+  return pace::act_entry<pace::GeluErfOp, true>(out, input, num_tokens, d, input_row_stride,
+                                                out_row_stride, dtype, stream, "gelu_and_mul");
+}
+
+extern "C" int pace_gelu_tanh_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                                      int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                                      cudaStream_t stream) {
+  return pace::act_entry<pace::GeluTanhOp, true>(out, input, num_tokens, d, input_row_stride,
+                                                 out_row_stride, dtype, stream,
+                                                 "gelu_tanh_and_mul");
+}
+
+extern "C" int pace_gelu_new(void* out, const void* input, int64_t num_tokens, int64_t d,
+                             int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                             cudaStream_t stream) {
+  return pace::act_entry<pace::GeluNewOp, false>(out, input, num_tokens, d, input_row_stride,
+                                                 out_row_stride, dtype, stream, "gelu_new");
+}
+
+extern "C" int pace_gelu_fast(void* out, const void* input, int64_t num_tokens, int64_t d,
+                              int64_t input_row_stride, int64_t out_row_stride, int dtype,
+                              cudaStream_t stream) {
+  return pace::act_entry<pace::GeluFastOp, false>(out, input, num_tokens, d, input_row_stride,
+                                                  out_row_stride, dtype, stream, "gelu_fast");
+}

@@ -1,0 +1,225 @@
+// RMSNorm and fused residual-add + RMSNorm for sm_100a.
+//
+// Semantics follow the reference kernel (csrc/layernorm_kernels.cu:10-35):
+// fp32 sum of squares, inv = rsqrtf(sum / H + eps), and the normalised value
+// is rounded to the storage type BEFORE the weight multiply
+// (out = (T)((T)(x * inv) * w), layernorm_kernels.cu:33).  The fused variant
+// restates the PyTorch composition at paceserve/model_executor/models/llama.py:
+// 248-252: residual <- (T)(x + residual), then rms_norm of that rounded sum.
+//
+// Design: one CTA per token row; the row is read once with 16-byte vectors and
+// held in registers across the reduction (the reference reads it twice with
+// 2-byte loads); warp-shuffle then shared-memory reduction, fixed order so all
+// threads derive the identical inv.  Rows that do not meet the vector
+// alignment go through a scalar two-pass kernel.
+#include "common.cuh"
+
+namespace pace {
+namespace {
+
+constexpr int kMaxThreads = 256;  // vector path: rows up to 8 x 256 vectors
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Sum of `v` over the CTA; every thread gets the same value.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float total = 0.f;
+  for (int i = 0; i < nwarps; ++i) total += red[i];
+  return total;
+}
+
+// Vector path.  NV = 16-byte vectors per thread (at most 8, so a row of up to
+// 2048 vectors -- H = 16384 in bf16 -- stays in registers).  FUSED: x_in == x_out is the
+// hidden-state row (read, then overwritten with the normalised row) and
+// `res` is the residual row (overwritten with x + res).
+template <typename T, int NV, bool FUSED>
+__global__ void __launch_bounds__(kMaxThreads)
+    rms_norm_vec_kernel(const T* x_in, T* x_out, T* res, const T* __restrict__ weight, float eps,
+                        int hidden, int64_t in_stride, int64_t out_stride, int64_t res_stride) {
+  using Tr = Traits<T>;
+  constexpr int V = Tr::kVec;
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+
+  const int64_t row = blockIdx.x;
+  const int nvec = hidden / V;
+  const T* xr = x_in + row * in_stride;
+  T* orow = x_out + row * out_stride;
+  T* rr = FUSED ? res + row * res_stride : nullptr;
+
+  float v[NV][V];
+  uint4 raw[NV];
+  uint4 rraw[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = threadIdx.x + j * blockDim.x;
+    if (c < nvec) {
+      if (FUSED) {
+        raw[j] = ld_v4(xr + (int64_t)c * V);
+        rraw[j] = ld_v4(rr + (int64_t)c * V);
+      } else {
+        raw[j] = ld_nc_v4(xr + (int64_t)c * V);
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = threadIdx.x + j * blockDim.x;
+    if (c < nvec) {
+      Tr::unpack(raw[j], v[j]);
+      if (FUSED) {
+        float r[V];
+        Tr::unpack(rraw[j], r);
+#pragma unroll
+        for (int e = 0; e < V; ++e) v[j][e] = Tr::round(v[j][e] + r[e]);
+        st_v4(rr + (int64_t)c * V, Tr::pack(v[j]));
+      }
+#pragma unroll
+      for (int e = 0; e < V; ++e) ss += v[j][e] * v[j][e];
+    }
+  }
+  const float total = block_sum(ss, red);
+  const float inv = rsqrtf(total / (float)hidden + eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = threadIdx.x + j * blockDim.x;
+    if (c < nvec) {
+      float w[V];
+      Tr::unpack(__ldg(reinterpret_cast<const uint4*>(weight) + c), w);
+      float o[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) o[e] = Tr::round(v[j][e] * inv) * w[e];
+      st_v4(orow + (int64_t)c * V, Tr::pack(o));
+    }
+  }
+}
+
+// Scalar fallback for any hidden size, stride or alignment.
+template <typename T, bool FUSED>
+__global__ void __launch_bounds__(256)
+    rms_norm_scalar_kernel(const T* x_in, T* x_out, T* res, const T* __restrict__ weight,
+                           float eps, int hidden, int64_t in_stride, int64_t out_stride,
+                           int64_t res_stride) {
+  using Tr = Traits<T>;
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const T* xr = x_in + row * in_stride;
+  T* orow = x_out + row * out_stride;
+  T* rr = FUSED ? res + row * res_stride : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float x = Tr::to_f(xr[i]);
+    if (FUSED) {
+      x = Tr::round(x + Tr::to_f(rr[i]));
+      rr[i] = Tr::from_f(x);
+    }
+    ss += x * x;
+  }
+  const float total = block_sum(ss, red);
+  const float inv = rsqrtf(total / (float)hidden + eps);
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    // Each thread re-reads only elements it read (and, fused, wrote) itself.
+    const float x = FUSED ? Tr::to_f(rr[i]) : Tr::to_f(xr[i]);
+    orow[i] = Tr::from_f(Tr::round(x * inv) * Tr::to_f(weight[i]));
+  }
+}
+
+template <typename T, bool FUSED>
+int launch_norm(const void* x_in, void* x_out, void* res, const void* weight, float eps,
+                int64_t num_tokens, int64_t hidden, int64_t in_stride, int64_t out_stride,
+                int64_t res_stride, cudaStream_t stream, const char* name) {
+  constexpr int V = Traits<T>::kVec;
+  const T* xi = static_cast<const T*>(x_in);
+  T* xo = static_cast<T*>(x_out);
+  T* r = static_cast<T*>(res);
+  const T* w = static_cast<const T*>(weight);
+  const int64_t nvec = hidden / V;
+  bool vec = (hidden % V == 0) && (in_stride % V == 0) && (out_stride % V == 0) &&
+             aligned16(x_in) && aligned16(x_out) && aligned16(weight) &&
+             nvec <= 8 * kMaxThreads;
+  if (FUSED) vec = vec && (res_stride % V == 0) && aligned16(res);
+  cudaError_t err;
+  const dim3 grid((unsigned)num_tokens);
+  if (vec) {
+    int nv = 1;
+    while (nv < 8 && ceil_div(nvec, nv) > kMaxThreads) nv *= 2;
+    int threads = (int)ceil_div(ceil_div(nvec, nv), 32) * 32;
+    if (threads > kMaxThreads) threads = kMaxThreads;
+    const int h = (int)hidden;
+    switch (nv) {
+#define PACE_NORM_CASE(N)                                                                     \
+  case N:                                                                                     \
+    err = launch(rms_norm_vec_kernel<T, N, FUSED>, grid, dim3(threads), 0, stream, xi, xo, r, \
+                 w, eps, h, in_stride, out_stride, res_stride);                               \
+    break;
+      PACE_NORM_CASE(1)
+      PACE_NORM_CASE(2)
+      PACE_NORM_CASE(4)
+      PACE_NORM_CASE(8)
+#undef PACE_NORM_CASE
+      default: return fail(PACE_ERR_INVALID_ARGUMENT, "%s: internal vector split", name);
+    }
+  } else {
+    err = launch(rms_norm_scalar_kernel<T, FUSED>, grid, dim3(256), 0, stream, xi, xo, r, w, eps,
+                 (int)hidden, in_stride, out_stride, res_stride);
+  }
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  return PACE_OK;
+}
+
+}  // namespace
+}  // namespace pace
+
+extern "C" int pace_rms_norm(void* out, const void* input, const void* weight, float epsilon,
+                             int64_t num_tokens, int64_t hidden_size, int64_t input_row_stride,
+                             int64_t out_row_stride, int dtype, cudaStream_t stream) {
+  using namespace pace;
+  if (num_tokens < 0 || hidden_size <= 0 || hidden_size > INT32_MAX || num_tokens > INT32_MAX)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "rms_norm: bad shape [%lld, %lld]",
+                (long long)num_tokens, (long long)hidden_size);
+  if (input_row_stride < hidden_size || out_row_stride < hidden_size)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "rms_norm: row stride smaller than hidden size");
+  if (num_tokens == 0) return PACE_OK;
+  if (!out || !input || !weight) return fail(PACE_ERR_INVALID_ARGUMENT, "rms_norm: null pointer");
+  StreamDeviceGuard guard(stream);
+  return PACE_DISPATCH_FLOAT(dtype, "rms_norm", [&] {
+    return launch_norm<scalar_t, false>(input, out, nullptr, weight, epsilon, num_tokens,
+                                        hidden_size, input_row_stride, out_row_stride, 0, stream,
+                                        "rms_norm");
+  });
+}
+
+extern "C" int pace_fused_add_rms_norm(void* input, void* residual, const void* weight,
+                                       float epsilon, int64_t num_tokens, int64_t hidden_size,
+                                       int64_t input_row_stride, int64_t residual_row_stride,
+                                       int dtype, cudaStream_t stream) {
+  using namespace pace;
+  if (num_tokens < 0 || hidden_size <= 0 || hidden_size > INT32_MAX || num_tokens > INT32_MAX)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "fused_add_rms_norm: bad shape [%lld, %lld]",
+                (long long)num_tokens, (long long)hidden_size);
+  if (input_row_stride < hidden_size || residual_row_stride < hidden_size)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "fused_add_rms_norm: row stride smaller than hidden size");
+  if (num_tokens == 0) return PACE_OK;
+  if (!input || !residual || !weight)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "fused_add_rms_norm: null pointer");
+  StreamDeviceGuard guard(stream);
+  return PACE_DISPATCH_FLOAT(dtype, "fused_add_rms_norm", [&] {
+    return launch_norm<scalar_t, true>(input, input, residual, weight, epsilon, num_tokens,
+                                       hidden_size, input_row_stride, input_row_stride,
+                                       residual_row_stride, stream, "fused_add_rms_norm");
+  });
+}

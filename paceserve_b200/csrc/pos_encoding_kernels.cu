@@ -1,0 +1,227 @@
+// In-place rotary position embedding on query and key for sm_100a.
+//
+// Semantics follow the reference (csrc/pos_encoding_kernels.cu:8-76): the
+// cache row for position p is [cos(rot_dim/2) | sin(rot_dim/2)]; GPT-NeoX style
+// rotates the pair (i, i + rot_dim/2) of every head, GPT-J style the pair
+// (2i, 2i+1), both with x' = x cos - y sin, y' = y cos + x sin; elements past
+// rot_dim in a head are untouched; q/k row strides are honoured (the q and k
+// views of a fused qkv projection).  Differences, by design: the math runs in
+// fp32 (the reference rounds every product to the storage type), the cache
+// may be fp32 while q/k are bf16/fp16, and a token whose position is outside
+// [0, max_position) is left unchanged instead of reading outside the cache.
+//
+// Design: one CTA per token; a thread owns one "unit" of one head: for NeoX a
+// 16-byte vector of the first half plus the matching vector of the second
+// half, for GPT-J one 16-byte vector of interleaved pairs, so every q/k access
+// is a coalesced 16-byte load/store and cos/sin are fetched as vectors too.
+#include "common.cuh"
+
+namespace pace {
+namespace {
+
+// N consecutive cache entries as floats, with one or two vector loads.
+template <typename C, int N>
+__device__ __forceinline__ void load_cs(const C* p, float* out) {
+  if constexpr (sizeof(C) == 4) {
+    static_assert(N == 8 || N == 4 || N == 2, "");
+    if constexpr (N == 8) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+      out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+      out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+    } else if constexpr (N == 4) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+      out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+    } else {
+      const float2 a = __ldg(reinterpret_cast<const float2*>(p));
+      out[0] = a.x; out[1] = a.y;
+    }
+  } else {
+    static_assert(N == 8 || N == 4, "");
+    if constexpr (N == 8) {
+      Traits<C>::unpack(__ldg(reinterpret_cast<const uint4*>(p)), out);
+    } else {
+      const uint2 a = __ldg(reinterpret_cast<const uint2*>(p));
+      float tmp[8];
+      Traits<C>::unpack(make_uint4(a.x, a.y, 0u, 0u), tmp);
+      out[0] = tmp[0]; out[1] = tmp[1]; out[2] = tmp[2]; out[3] = tmp[3];
+    }
+  }
+}
+
+template <typename T, typename C, bool NEOX>
+__global__ void __launch_bounds__(512)
+    rope_vec_kernel(const int64_t* __restrict__ positions, T* query, T* key, int num_heads,
+                    int num_kv_heads, int head_size, int64_t q_stride, int64_t k_stride,
+                    const C* __restrict__ cache, int rot_dim, int64_t max_position) {
+  using Tr = Traits<T>;
+  constexpr int V = Tr::kVec;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t tok = blockIdx.x;
+  const int64_t pos = positions[tok];
+  if (pos < 0 || pos >= max_position) return;
+  const int embed = rot_dim / 2;
+  // units per head: NeoX pairs a vector of each half; GPT-J one vector of pairs
+  const int uph = NEOX ? embed / V : rot_dim / V;
+  const int total = (num_heads + num_kv_heads) * uph;
+  const C* cos_row = cache + pos * rot_dim;
+  const C* sin_row = cos_row + embed;
+  for (int u = threadIdx.x; u < total; u += blockDim.x) {
+    const int head = u / uph;
+    const int part = u - head * uph;
+    T* hp = head < num_heads ? query + tok * q_stride + (int64_t)head * head_size
+                             : key + tok * k_stride + (int64_t)(head - num_heads) * head_size;
+    if (NEOX) {
+      const int i0 = part * V;
+      float c[V], s[V], x[V], y[V];
+      const uint4 xv = ld_v4(hp + i0);
+      const uint4 yv = ld_v4(hp + embed + i0);
+      load_cs<C, V>(cos_row + i0, c);
+      load_cs<C, V>(sin_row + i0, s);
+      Tr::unpack(xv, x);
+      Tr::unpack(yv, y);
+      float xo[V], yo[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        xo[e] = x[e] * c[e] - y[e] * s[e];
+        yo[e] = y[e] * c[e] + x[e] * s[e];
+      }
+      st_v4(hp + i0, Tr::pack(xo));
+      st_v4(hp + embed + i0, Tr::pack(yo));
+    } else {
+      const int e0 = part * V;  // element offset; pairs e0/2 .. e0/2 + V/2
+      float c[V / 2], s[V / 2], a[V];
+      const uint4 av = ld_v4(hp + e0);
+      load_cs<C, V / 2>(cos_row + e0 / 2, c);
+      load_cs<C, V / 2>(sin_row + e0 / 2, s);
+      Tr::unpack(av, a);
+      float o[V];
+#pragma unroll
+      for (int p = 0; p < V / 2; ++p) {
+        const float x = a[2 * p], y = a[2 * p + 1];
+        o[2 * p] = x * c[p] - y * s[p];
+        o[2 * p + 1] = y * c[p] + x * s[p];
+      }
+      st_v4(hp + e0, Tr::pack(o));
+    }
+  }
+}
+
+// Scalar fallback: one thread per rotated pair.
+template <typename T, typename C, bool NEOX>
+__global__ void __launch_bounds__(256)
+    rope_scalar_kernel(const int64_t* __restrict__ positions, T* query, T* key, int num_heads,
+                       int num_kv_heads, int head_size, int64_t q_stride, int64_t k_stride,
+                       const C* __restrict__ cache, int rot_dim, int64_t max_position) {
+  using Tr = Traits<T>;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t tok = blockIdx.x;
+  const int64_t pos = positions[tok];
+  if (pos < 0 || pos >= max_position) return;
+  const int embed = rot_dim / 2;
+  const int total = (num_heads + num_kv_heads) * embed;
+  const C* cos_row = cache + pos * rot_dim;
+  const C* sin_row = cos_row + embed;
+  for (int u = threadIdx.x; u < total; u += blockDim.x) {
+    const int head = u / embed;
+    const int i = u - head * embed;
+    T* hp = head < num_heads ? query + tok * q_stride + (int64_t)head * head_size
+                             : key + tok * k_stride + (int64_t)(head - num_heads) * head_size;
+    const int xi = NEOX ? i : 2 * i;
+    const int yi = NEOX ? embed + i : 2 * i + 1;
+    const float c = Traits<C>::to_f(cos_row[i]);
+    const float s = Traits<C>::to_f(sin_row[i]);
+    const float x = Tr::to_f(hp[xi]);
+    const float y = Tr::to_f(hp[yi]);
+    hp[xi] = Tr::from_f(x * c - y * s);
+    hp[yi] = Tr::from_f(y * c + x * s);
+  }
+}
+
+template <typename T, typename C>
+int launch_rope(const int64_t* positions, void* query, void* key, int64_t num_tokens,
+                int num_heads, int num_kv_heads, int head_size, int64_t q_stride,
+                int64_t k_stride, const void* cache, int rot_dim, int64_t max_position,
+                bool neox, cudaStream_t stream) {
+  constexpr int V = Traits<T>::kVec;
+  T* q = static_cast<T*>(query);
+  T* k = static_cast<T*>(key);
+  const C* cs = static_cast<const C*>(cache);
+  const int embed = rot_dim / 2;
+  bool vec = (head_size % V == 0) && (q_stride % V == 0) && aligned16(query) &&
+             aligned16(cache) && ((int64_t)rot_dim * (int64_t)sizeof(C)) % 16 == 0;
+  if (num_kv_heads > 0) vec = vec && (k_stride % V == 0) && aligned16(key);
+  if (neox)
+    vec = vec && (embed % V == 0);
+  else
+    vec = vec && (rot_dim % V == 0);
+  const dim3 grid((unsigned)num_tokens);
+  cudaError_t err;
+  if (vec) {
+    const int uph = neox ? embed / V : rot_dim / V;
+    int threads = (int)ceil_div((int64_t)(num_heads + num_kv_heads) * uph, 32) * 32;
+    if (threads > 512) threads = 512;
+    if (threads < 32) threads = 32;
+    err = neox ? launch(rope_vec_kernel<T, C, true>, grid, dim3(threads), 0, stream, positions, q,
+                        k, num_heads, num_kv_heads, head_size, q_stride, k_stride, cs, rot_dim,
+                        max_position)
+               : launch(rope_vec_kernel<T, C, false>, grid, dim3(threads), 0, stream, positions,
+                        q, k, num_heads, num_kv_heads, head_size, q_stride, k_stride, cs, rot_dim,
+                        max_position);
+  } else {
+    err = neox ? launch(rope_scalar_kernel<T, C, true>, grid, dim3(256), 0, stream, positions, q,
+                        k, num_heads, num_kv_heads, head_size, q_stride, k_stride, cs, rot_dim,
+                        max_position)
+               : launch(rope_scalar_kernel<T, C, false>, grid, dim3(256), 0, stream, positions,
+                        q, k, num_heads, num_kv_heads, head_size, q_stride, k_stride, cs, rot_dim,
+                        max_position);
+  }
+  if (err != cudaSuccess) return cuda_fail(err, "rotary_embedding");
+  return PACE_OK;
+}
+
+}  // namespace
+}  // namespace pace
+
+extern "C" int pace_rotary_embedding(const int64_t* positions, void* query, void* key,
+                                     int64_t num_tokens, int num_heads, int num_kv_heads,
+                                     int head_size, int64_t query_row_stride,
+                                     int64_t key_row_stride, const void* cos_sin_cache,
+                                     int cache_dtype, int rot_dim, int64_t max_position,
+                                     int is_neox, int dtype, cudaStream_t stream) {
+  using namespace pace;
+  if (num_tokens < 0 || num_tokens > INT32_MAX || num_heads < 0 || num_kv_heads < 0 ||
+      head_size <= 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "rotary_embedding: bad shape");
+  if (rot_dim <= 0 || rot_dim % 2 != 0 || rot_dim > head_size)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "rotary_embedding: rot_dim %d must be even and in (0, head_size=%d]", rot_dim,
+                head_size);
+  if (max_position <= 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "rotary_embedding: empty cos_sin_cache");
+  if (query_row_stride < (int64_t)num_heads * head_size ||
+      (num_kv_heads > 0 && key_row_stride < (int64_t)num_kv_heads * head_size))
+    return fail(PACE_ERR_INVALID_ARGUMENT, "rotary_embedding: row stride smaller than the row");
+  if (num_tokens == 0 || num_heads + num_kv_heads == 0) return PACE_OK;
+  if (!positions || !cos_sin_cache || (num_heads > 0 && !query) || (num_kv_heads > 0 && !key))
+    return fail(PACE_ERR_INVALID_ARGUMENT, "rotary_embedding: null pointer");
+  StreamDeviceGuard guard(stream);
+  const bool neox = is_neox != 0;
+  return PACE_DISPATCH_FLOAT(dtype, "rotary_embedding", [&] {
+    if (cache_dtype == PACE_F32)
+      return launch_rope<scalar_t, float>(positions, query, key, num_tokens, num_heads,
+                                          num_kv_heads, head_size, query_row_stride,
+                                          key_row_stride, cos_sin_cache, rot_dim, max_position,
+                                          neox, stream);
+    if (cache_dtype == dtype)
+      return launch_rope<scalar_t, scalar_t>(positions, query, key, num_tokens, num_heads,
+                                             num_kv_heads, head_size, query_row_stride,
+                                             key_row_stride, cos_sin_cache, rot_dim,
+                                             max_position, neox, stream);
+    return fail(PACE_ERR_UNSUPPORTED_DTYPE,
+                "rotary_embedding: cos_sin_cache dtype %d must be float32 or the q/k dtype %d",
+                cache_dtype, dtype);
+  });
+}

@@ -1,0 +1,514 @@
+// Thin torch extension over the C ABI (include/pace_b200.h).  It recreates
+// the reference's four pybind modules with their exact signatures
+// (csrc/layernorm.cpp:3-14, csrc/pos_encoding.cpp:3-16,
+// csrc/activation.cpp:3-28, csrc/moe.cpp:3-28) as submodules
+// layernorm_ops / pos_encoding_ops / activation_ops / moe_ops of
+// paceserve_b200._C, adds the new ops (fused_add_rms_norm, gelu_and_mul,
+// gelu_tanh_and_mul) in the same style, and a kv_transfer_ops submodule for
+// the paged-KV block copy.  Tensors are validated here; every launch goes
+// through the C ABI on the current stream of the tensors' device, and a
+// non-zero status becomes a RuntimeError carrying pace_last_error().
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <string>
+#include <vector>
+
+#include "pace_b200.h"
+
+namespace {
+
+using torch::Tensor;
+
+int pace_dtype(const Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return PACE_F32;
+    case at::kHalf: return PACE_F16;
+    case at::kBFloat16: return PACE_BF16;
+    case at::kByte: return PACE_U8;
+    case at::kChar: return PACE_I8;
+    case at::kShort: return PACE_I16;
+    case at::kInt: return PACE_I32;
+    case at::kLong: return PACE_I64;
+    default: return -1;
+  }
+}
+
+void check_status(int rc, const char* op) {
+  TORCH_CHECK(rc == PACE_OK, op, " failed (", pace_status_string(rc), "): ", pace_last_error());
+}
+
+cudaStream_t stream_of(const Tensor& t) {
+  return at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+void check_cuda(const Tensor& t, const char* op, const char* name) {
+  TORCH_CHECK(t.is_cuda(), op, ": ", name, " must be a CUDA tensor");
+}
+
+void check_same_device(const Tensor& a, const Tensor& b, const char* op) {
+  TORCH_CHECK(a.device() == b.device(), op, ": tensors on different devices (", a.device(), " vs ",
+              b.device(), ")");
+}
+
+bool is_float_type(const Tensor& t) {
+  return t.scalar_type() == at::kFloat || t.scalar_type() == at::kHalf ||
+         t.scalar_type() == at::kBFloat16;
+}
+
+// Row view of a tensor whose last dimension is contiguous: (rows, width,
+// row_stride).  2-D tensors may have any row stride; higher ranks must be
+// collapsible into rows with a single stride.
+struct Rows {
+  int64_t rows, width, stride;
+};
+
+Rows rows_of(const Tensor& t, const char* op, const char* name) {
+  TORCH_CHECK(t.dim() >= 1, op, ": ", name, " must have at least one dimension");
+  const int64_t w = t.size(-1);
+  TORCH_CHECK(t.numel() == 0 || w == 1 || t.stride(-1) == 1, op, ": ", name,
+              " must be contiguous in its last dimension");
+  if (t.dim() == 1) return {1, w, w};
+  if (t.dim() == 2) return {t.size(0), w, t.size(0) <= 1 ? w : t.stride(0)};
+  TORCH_CHECK(t.is_contiguous(), op, ": ", name, " of rank > 2 must be contiguous");
+  return {w == 0 ? 0 : t.numel() / w, w, w};
+}
+
+// ------------------------------------------------------------- layernorm --
+void rms_norm(Tensor& out, Tensor& input, Tensor& weight, double epsilon) {
+  const char* op = "rms_norm";
+  check_cuda(input, op, "input");
+  check_same_device(out, input, op);
+  check_same_device(weight, input, op);
+  TORCH_CHECK(is_float_type(input), op, ": input dtype must be float32, float16 or bfloat16");
+  TORCH_CHECK(out.scalar_type() == input.scalar_type() && weight.scalar_type() == input.scalar_type(),
+              op, ": out, input and weight must share a dtype");
+  const Rows in = rows_of(input, op, "input");
+  const Rows o = rows_of(out, op, "out");
+  TORCH_CHECK(o.rows == in.rows && o.width == in.width, op, ": out shape ", out.sizes(),
+              " does not match input ", input.sizes());
+  TORCH_CHECK(weight.is_contiguous() && weight.numel() == in.width, op, ": weight must be [",
+              in.width, "] and contiguous");
+  const at::cuda::CUDAGuard guard(input.device());
+  check_status(pace_rms_norm(out.data_ptr(), input.data_ptr(), weight.data_ptr(), (float)epsilon,
+                             in.rows, in.width, in.stride, o.stride, pace_dtype(input),
+                             stream_of(input)),
+               op);
+}
+
+void fused_add_rms_norm(Tensor& input, Tensor& residual, Tensor& weight, double epsilon) {
+  const char* op = "fused_add_rms_norm";
+  check_cuda(input, op, "input");
+  check_same_device(residual, input, op);
+  check_same_device(weight, input, op);
+  TORCH_CHECK(is_float_type(input), op, ": input dtype must be float32, float16 or bfloat16");
+  TORCH_CHECK(residual.scalar_type() == input.scalar_type() &&
+                  weight.scalar_type() == input.scalar_type(),
+              op, ": input, residual and weight must share a dtype");
+  const Rows in = rows_of(input, op, "input");
+  const Rows r = rows_of(residual, op, "residual");
+  TORCH_CHECK(r.rows == in.rows && r.width == in.width, op, ": residual shape ", residual.sizes(),
+              " does not match input ", input.sizes());
+  TORCH_CHECK(weight.is_contiguous() && weight.numel() == in.width, op, ": weight must be [",
+              in.width, "] and contiguous");
+  const at::cuda::CUDAGuard guard(input.device());
+  check_status(pace_fused_add_rms_norm(input.data_ptr(), residual.data_ptr(), weight.data_ptr(),
+                                       (float)epsilon, in.rows, in.width, in.stride, r.stride,
+                                       pace_dtype(input), stream_of(input)),
+               op);
+}
+
+// ---------------------------------------------------------- pos encoding --
+// q/k as [T, heads * head_size] (any row stride) or [T, heads, head_size].
+Rows qk_rows(const Tensor& t, int64_t head_size, const char* op, const char* name) {
+  TORCH_CHECK(t.dim() == 2 || t.dim() == 3, op, ": ", name, " must be 2-D or 3-D");
+  TORCH_CHECK(t.size(-1) <= 1 || t.stride(-1) == 1, op, ": ", name,
+              " must be contiguous in its last dimension");
+  if (t.dim() == 3) {
+    TORCH_CHECK(t.size(2) == head_size, op, ": ", name, " last dim must equal head_size");
+    TORCH_CHECK(t.size(1) <= 1 || t.stride(1) == head_size, op, ": ", name,
+                " heads must be contiguous");
+    return {t.size(0), t.size(1) * head_size, t.size(0) <= 1 ? t.size(1) * head_size : t.stride(0)};
+  }
+  TORCH_CHECK(t.size(1) % head_size == 0, op, ": ", name, " width ", t.size(1),
+              " is not a multiple of head_size ", head_size);
+  return {t.size(0), t.size(1), t.size(0) <= 1 ? t.size(1) : t.stride(0)};
+}
+
+void rotary_embedding(Tensor& positions, Tensor& query, Tensor& key, int64_t head_size,
+                      Tensor& cos_sin_cache, bool is_neox) {
+  const char* op = "rotary_embedding";
+  check_cuda(query, op, "query");
+  check_same_device(positions, query, op);
+  check_same_device(key, query, op);
+  check_same_device(cos_sin_cache, query, op);
+  TORCH_CHECK(head_size > 0, op, ": head_size must be positive");
+  TORCH_CHECK(is_float_type(query) && key.scalar_type() == query.scalar_type(), op,
+              ": query and key must share a float dtype");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && positions.is_contiguous(), op,
+              ": positions must be a contiguous int64 tensor");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(), op,
+              ": cos_sin_cache must be a contiguous [max_position, rot_dim] tensor");
+  TORCH_CHECK(cos_sin_cache.scalar_type() == at::kFloat ||
+                  cos_sin_cache.scalar_type() == query.scalar_type(),
+              op, ": cos_sin_cache must be float32 or the query dtype");
+  const Rows q = qk_rows(query, head_size, op, "query");
+  const Rows k = qk_rows(key, head_size, op, "key");
+  TORCH_CHECK(k.rows == q.rows, op, ": query and key token counts differ");
+  TORCH_CHECK(positions.numel() >= q.rows, op, ": positions has ", positions.numel(),
+              " entries for ", q.rows, " tokens");
+  const at::cuda::CUDAGuard guard(query.device());
+  check_status(pace_rotary_embedding(
+                   positions.data_ptr<int64_t>(), query.data_ptr(), key.data_ptr(), q.rows,
+                   (int)(q.width / head_size), (int)(k.width / head_size), (int)head_size,
+                   q.stride, k.stride, cos_sin_cache.data_ptr(), pace_dtype(cos_sin_cache),
+                   (int)cos_sin_cache.size(1), cos_sin_cache.size(0), is_neox ? 1 : 0,
+                   pace_dtype(query), stream_of(query)),
+               op);
+}
+
+// ------------------------------------------------------------ activation --
+using ActFn = int (*)(void*, const void*, int64_t, int64_t, int64_t, int64_t, int, cudaStream_t);
+
+void activation(Tensor& out, Tensor& input, ActFn fn, bool gated, const char* op) {
+  check_cuda(input, op, "input");
+  check_same_device(out, input, op);
+  TORCH_CHECK(is_float_type(input) && out.scalar_type() == input.scalar_type(), op,
+              ": out and input must share a float dtype");
+  const Rows in = rows_of(input, op, "input");
+  const Rows o = rows_of(out, op, "out");
+  const int64_t d = gated ? in.width / 2 : in.width;
+  TORCH_CHECK(!gated || in.width % 2 == 0, op, ": input width must be even");
+  TORCH_CHECK(o.rows == in.rows && o.width == d, op, ": out shape ", out.sizes(),
+              " does not match input ", input.sizes());
+  const at::cuda::CUDAGuard guard(input.device());
+  check_status(fn(out.data_ptr(), input.data_ptr(), in.rows, d, in.stride, o.stride,
+                  pace_dtype(input), stream_of(input)),
+               op);
+}
+
+void silu_and_mul(Tensor& out, Tensor& input) {
+  activation(out, input, pace_silu_and_mul, true, "silu_and_mul");
+}
+void gelu_and_mul(Tensor& out, Tensor& input) {
+  activation(out, input, pace_gelu_and_mul, true, "gelu_and_mul");
+}
+void gelu_tanh_and_mul(Tensor& out, Tensor& input) {
+  activation(out, input, pace_gelu_tanh_and_mul, true, "gelu_tanh_and_mul");
+}
+void gelu_new(Tensor& out, Tensor& input) {
+  activation(out, input, pace_gelu_new, false, "gelu_new");
+}
+void gelu_fast(Tensor& out, Tensor& input) {
+  activation(out, input, pace_gelu_fast, false, "gelu_fast");
+}
+
+// ------------------------------------------------------------------- moe --
+void topk_softmax(Tensor& topk_weights, Tensor& topk_indices, Tensor& token_expert_indices,
+                  Tensor& gating_output, bool renormalize) {
+  const char* op = "topk_softmax";
+  check_cuda(gating_output, op, "gating_output");
+  check_same_device(topk_weights, gating_output, op);
+  check_same_device(topk_indices, gating_output, op);
+  check_same_device(token_expert_indices, gating_output, op);
+  TORCH_CHECK(gating_output.scalar_type() == at::kFloat && gating_output.is_contiguous(), op,
+              ": gating_output must be a contiguous float32 tensor");
+  TORCH_CHECK(topk_weights.scalar_type() == at::kFloat && topk_weights.is_contiguous(), op,
+              ": topk_weights must be a contiguous float32 tensor");
+  TORCH_CHECK(topk_indices.scalar_type() == at::kInt && topk_indices.is_contiguous() &&
+                  token_expert_indices.scalar_type() == at::kInt &&
+                  token_expert_indices.is_contiguous(),
+              op, ": topk_indices and token_expert_indices must be contiguous int32 tensors");
+  const int64_t E = gating_output.size(-1);
+  TORCH_CHECK(E > 0, op, ": no experts");
+  const int64_t T = gating_output.numel() / E;
+  const int64_t k = topk_weights.size(-1);
+  TORCH_CHECK(topk_weights.numel() == T * k && topk_indices.numel() == T * k &&
+                  token_expert_indices.numel() == T * k,
+              op, ": outputs must hold [", T, ", ", k, "]");
+  const at::cuda::CUDAGuard guard(gating_output.device());
+  check_status(pace_topk_softmax(topk_weights.data_ptr<float>(), topk_indices.data_ptr<int32_t>(),
+                                 token_expert_indices.data_ptr<int32_t>(),
+                                 gating_output.data_ptr<float>(), T, (int)E, (int)k,
+                                 renormalize ? 1 : 0, stream_of(gating_output)),
+               op);
+}
+
+void moe_align_block_size(Tensor topk_ids, int64_t num_experts, int64_t block_size,
+                          Tensor sorted_token_ids, Tensor experts_ids, Tensor num_tokens_post_pad,
+                          bool fill_padding) {
+  const char* op = "moe_align_block_size";
+  check_cuda(topk_ids, op, "topk_ids");
+  check_same_device(sorted_token_ids, topk_ids, op);
+  check_same_device(experts_ids, topk_ids, op);
+  check_same_device(num_tokens_post_pad, topk_ids, op);
+  const int dt = pace_dtype(topk_ids);
+  TORCH_CHECK(dt >= PACE_U8 && dt <= PACE_I64, op, ": topk_ids must have an integral dtype");
+  TORCH_CHECK(topk_ids.is_contiguous(), op, ": topk_ids must be contiguous");
+  for (const Tensor* t : {&sorted_token_ids, &experts_ids, &num_tokens_post_pad})
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->is_contiguous(), op,
+                ": outputs must be contiguous int32 tensors");
+  TORCH_CHECK(num_tokens_post_pad.numel() >= 1, op, ": num_tokens_post_pad is empty");
+  TORCH_CHECK(num_experts > 0 && num_experts <= INT32_MAX && block_size > 0 &&
+                  block_size <= INT32_MAX,
+              op, ": num_experts and block_size must be positive int32 values");
+  const at::cuda::CUDAGuard guard(topk_ids.device());
+  check_status(pace_moe_align_block_size(
+                   topk_ids.data_ptr(), dt, topk_ids.numel(), (int)num_experts, (int)block_size,
+                   sorted_token_ids.data_ptr<int32_t>(), sorted_token_ids.numel(),
+                   experts_ids.data_ptr<int32_t>(), experts_ids.numel(),
+                   num_tokens_post_pad.data_ptr<int32_t>(), fill_padding ? 1 : 0,
+                   stream_of(topk_ids)),
+               op);
+}
+
+// ------------------------------------------------------------ kv transfer --
+struct CacheSet {
+  std::vector<void*> ptrs;
+  int64_t num_blocks = 0;
+  int64_t block_bytes = 0;
+  c10::Device device = c10::Device(c10::kCPU);
+};
+
+CacheSet cache_set(const std::vector<Tensor>& caches, const char* op, const char* name) {
+  TORCH_CHECK(!caches.empty(), op, ": ", name, " is empty");
+  CacheSet s;
+  s.device = caches[0].device();
+  for (const Tensor& c : caches) {
+    TORCH_CHECK(c.is_cuda() && c.device() == s.device, op, ": ", name,
+                " must be CUDA tensors on one device");
+    TORCH_CHECK(c.is_contiguous() && c.dim() >= 1, op, ": ", name, " must be contiguous");
+    const int64_t nb = c.size(0);
+    const int64_t bb = nb == 0 ? 0 : (int64_t)(c.numel() / nb) * (int64_t)c.element_size();
+    if (s.ptrs.empty()) {
+      s.num_blocks = nb;
+      s.block_bytes = bb;
+    }
+    TORCH_CHECK(nb == s.num_blocks && bb == s.block_bytes, op, ": ", name,
+                " layers differ in shape");
+    s.ptrs.push_back(c.data_ptr());
+  }
+  return s;
+}
+
+Tensor ids_on(const Tensor& ids, const c10::Device& dev, const char* op, const char* name) {
+  TORCH_CHECK(ids.dim() == 1, op, ": ", name, " must be 1-D");
+  TORCH_CHECK(ids.scalar_type() == at::kInt || ids.scalar_type() == at::kLong, op, ": ", name,
+              " must be int32 or int64");
+  return ids.to(dev, at::kInt, /*non_blocking=*/false, /*copy=*/false).contiguous();
+}
+
+void run_kv_copy(const std::vector<void*>& src, const std::vector<void*>& dst,
+                 int64_t src_blocks, int64_t dst_blocks, int64_t block_bytes,
+                 const c10::Device& exec, const Tensor& src_ids, const Tensor& dst_ids,
+                 int64_t method, const c10::optional<Tensor>& bad_pairs, const char* op) {
+  TORCH_CHECK(src.size() == dst.size(), op, ": source and destination layer counts differ (",
+              src.size(), " vs ", dst.size(), ")");
+  const at::cuda::CUDAGuard guard(exec);
+  Tensor s = ids_on(src_ids, exec, op, "src_block_ids");
+  Tensor d = ids_on(dst_ids, exec, op, "dst_block_ids");
+  TORCH_CHECK(s.numel() == d.numel(), op, ": block id lists differ in length");
+  int32_t* bad = nullptr;
+  if (bad_pairs.has_value()) {
+    TORCH_CHECK(bad_pairs->scalar_type() == at::kInt && bad_pairs->device() == exec &&
+                    bad_pairs->numel() >= 1,
+                op, ": bad_pairs must be an int32 tensor on the executing device");
+    bad = bad_pairs->data_ptr<int32_t>();
+  }
+  check_status(pace_kv_copy_blocks(src.data(), dst.data(), (int)src.size(),
+                                   s.data_ptr<int32_t>(), d.data_ptr<int32_t>(), s.numel(),
+                                   block_bytes, src_blocks, dst_blocks, bad, (int)method,
+                                   at::cuda::getCurrentCUDAStream(exec.index()).stream()),
+               op);
+  // Device copies of the ids were allocated on this same stream, so the
+  // caching allocator cannot hand their memory out before the kernel ran.
+}
+
+// Copy blocks between two lists of per-layer caches (same or different GPUs).
+// Runs on the destination device (pull) unless push=True.
+void copy_blocks_p2p(const std::vector<Tensor>& src_caches, const std::vector<Tensor>& dst_caches,
+                     const Tensor& src_block_ids, const Tensor& dst_block_ids, int64_t method,
+                     bool push, const c10::optional<Tensor>& bad_pairs) {
+  const char* op = "copy_blocks_p2p";
+  CacheSet s = cache_set(src_caches, op, "src_caches");
+  CacheSet d = cache_set(dst_caches, op, "dst_caches");
+  TORCH_CHECK(s.block_bytes == d.block_bytes, op, ": source and destination block sizes differ");
+  const c10::Device exec = push ? s.device : d.device;
+  const c10::Device other = push ? d.device : s.device;
+  if (exec != other)
+    check_status(pace_enable_peer_access(exec.index(), other.index()), op);
+  run_kv_copy(s.ptrs, d.ptrs, s.num_blocks, d.num_blocks, s.block_bytes, exec, src_block_ids,
+              dst_block_ids, method, bad_pairs, op);
+}
+
+// Same, with the source given as raw per-layer pointers (e.g. mapped from
+// another process with ipc_open_handle) of src_num_blocks blocks each.
+void copy_blocks_from_ptrs(const std::vector<int64_t>& src_ptrs, int64_t src_num_blocks,
+                           const std::vector<Tensor>& dst_caches, const Tensor& src_block_ids,
+                           const Tensor& dst_block_ids, int64_t method,
+                           const c10::optional<Tensor>& bad_pairs) {
+  const char* op = "copy_blocks_from_ptrs";
+  CacheSet d = cache_set(dst_caches, op, "dst_caches");
+  std::vector<void*> s;
+  for (int64_t p : src_ptrs) s.push_back(reinterpret_cast<void*>(p));
+  run_kv_copy(s, d.ptrs, src_num_blocks, d.num_blocks, d.block_bytes, d.device, src_block_ids,
+              dst_block_ids, method, bad_pairs, op);
+}
+
+// Destination given as raw pointers (push into another process's cache).
+void copy_blocks_to_ptrs(const std::vector<Tensor>& src_caches, const std::vector<int64_t>& dst_ptrs,
+                         int64_t dst_num_blocks, const Tensor& src_block_ids,
+                         const Tensor& dst_block_ids, int64_t method,
+                         const c10::optional<Tensor>& bad_pairs) {
+  const char* op = "copy_blocks_to_ptrs";
+  CacheSet s = cache_set(src_caches, op, "src_caches");
+  std::vector<void*> d;
+  for (int64_t p : dst_ptrs) d.push_back(reinterpret_cast<void*>(p));
+  run_kv_copy(s.ptrs, d, s.num_blocks, dst_num_blocks, s.block_bytes, s.device, src_block_ids,
+              dst_block_ids, method, bad_pairs, op);
+}
+
+// out[l, j] = caches[l][block_ids[j]]; out is [L, n, ...] on the caches'
+// device or pinned host memory.
+void gather_blocks(const std::vector<Tensor>& caches, const Tensor& block_ids, Tensor& out,
+                   const c10::optional<Tensor>& bad_ids) {
+  const char* op = "gather_blocks";
+  CacheSet c = cache_set(caches, op, "caches");
+  const at::cuda::CUDAGuard guard(c.device);
+  Tensor ids = ids_on(block_ids, c.device, op, "block_ids");
+  TORCH_CHECK(out.is_contiguous(), op, ": out must be contiguous");
+  TORCH_CHECK(out.is_cuda() ? out.device() == c.device : out.is_pinned(), op,
+              ": out must live on the caches' device or in pinned host memory");
+  TORCH_CHECK((int64_t)out.numel() * out.element_size() ==
+                  (int64_t)c.ptrs.size() * ids.numel() * c.block_bytes,
+              op, ": out must hold num_layers * len(block_ids) blocks");
+  int32_t* bad = bad_ids.has_value() ? bad_ids->data_ptr<int32_t>() : nullptr;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(c.device.index()).stream();
+  check_status(pace_kv_gather_blocks(c.ptrs.data(), (int)c.ptrs.size(), ids.data_ptr<int32_t>(),
+                                     ids.numel(), c.block_bytes, c.num_blocks, out.data_ptr(), bad,
+                                     st),
+               op);
+}
+
+// caches[l][block_ids[j]] = src[l, j]
+void scatter_blocks(const Tensor& src, const std::vector<Tensor>& caches, const Tensor& block_ids,
+                    const c10::optional<Tensor>& bad_ids) {
+  const char* op = "scatter_blocks";
+  CacheSet c = cache_set(caches, op, "caches");
+  const at::cuda::CUDAGuard guard(c.device);
+  Tensor ids = ids_on(block_ids, c.device, op, "block_ids");
+  TORCH_CHECK(src.is_contiguous(), op, ": src must be contiguous");
+  TORCH_CHECK(src.is_cuda() ? src.device() == c.device : src.is_pinned(), op,
+              ": src must live on the caches' device or in pinned host memory");
+  TORCH_CHECK((int64_t)src.numel() * src.element_size() ==
+                  (int64_t)c.ptrs.size() * ids.numel() * c.block_bytes,
+              op, ": src must hold num_layers * len(block_ids) blocks");
+  int32_t* bad = bad_ids.has_value() ? bad_ids->data_ptr<int32_t>() : nullptr;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(c.device.index()).stream();
+  check_status(pace_kv_scatter_blocks(src.data_ptr(), c.ptrs.data(), (int)c.ptrs.size(),
+                                      ids.data_ptr<int32_t>(), ids.numel(), c.block_bytes,
+                                      c.num_blocks, bad, st),
+               op);
+}
+
+py::tuple ipc_get_handle(const Tensor& t) {
+  TORCH_CHECK(t.is_cuda(), "ipc_get_handle: tensor must be on a CUDA device");
+  const at::cuda::CUDAGuard guard(t.device());
+  char h[PACE_IPC_HANDLE_BYTES];
+  int64_t off = 0;
+  check_status(pace_ipc_get_handle(t.data_ptr(), h, &off), "ipc_get_handle");
+  return py::make_tuple(py::bytes(h, PACE_IPC_HANDLE_BYTES), off);
+}
+
+int64_t ipc_open_handle(const py::bytes& handle, int64_t device) {
+  std::string h = handle;
+  TORCH_CHECK(h.size() == PACE_IPC_HANDLE_BYTES, "ipc_open_handle: handle must be ",
+              PACE_IPC_HANDLE_BYTES, " bytes");
+  void* base = nullptr;
+  check_status(pace_ipc_open_handle(h.data(), (int)device, &base), "ipc_open_handle");
+  return reinterpret_cast<int64_t>(base);
+}
+
+void ipc_close_handle(int64_t base) {
+  check_status(pace_ipc_close_handle(reinterpret_cast<void*>(base)), "ipc_close_handle");
+}
+
+void enable_peer_access(int64_t device, int64_t peer) {
+  check_status(pace_enable_peer_access((int)device, (int)peer), "enable_peer_access");
+}
+
+bool can_access_peer(int64_t device, int64_t peer) {
+  int can = 0;
+  check_status(pace_can_access_peer((int)device, (int)peer, &can), "can_access_peer");
+  return can != 0;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_C, m) {
+  m.doc() = "PaceServe per-layer ops and KV transfer on B200 (sm_100a)";
+  m.def("version", &pace_version);
+  m.def("set_pdl", [](bool on) { pace_set_pdl(on ? 1 : 0); },
+        "Enable/disable programmatic dependent launch for the per-layer ops.");
+  m.def("get_pdl", []() { return pace_get_pdl() != 0; });
+
+  auto ln = m.def_submodule("layernorm_ops");
+  ln.def("rms_norm", &rms_norm, "Apply Root Mean Square (RMS) Normalization to the input tensor.",
+         py::arg("out"), py::arg("input"), py::arg("weight"), py::arg("epsilon"));
+  ln.def("fused_add_rms_norm", &fused_add_rms_norm,
+         "In place: residual += input; input = rms_norm(residual) * weight.", py::arg("input"),
+         py::arg("residual"), py::arg("weight"), py::arg("epsilon"));
+
+  auto pe = m.def_submodule("pos_encoding_ops");
+  pe.def("rotary_embedding", &rotary_embedding,
+         "Apply GPT-NeoX or GPT-J style rotary embedding to query and key", py::arg("positions"),
+         py::arg("query"), py::arg("key"), py::arg("head_size"), py::arg("cos_sin_cache"),
+         py::arg("is_neox"));
+
+  auto act = m.def_submodule("activation_ops");
+  act.def("silu_and_mul", &silu_and_mul, "Activation function used in SwiGLU.", py::arg("out"),
+          py::arg("input"));
+  act.def("gelu_and_mul", &gelu_and_mul, "GeGLU: gelu(x[:, :d]) * x[:, d:] (erf GELU).",
+          py::arg("out"), py::arg("input"));
+  act.def("gelu_tanh_and_mul", &gelu_tanh_and_mul,
+          "GeGLU with the tanh-approximated GELU.", py::arg("out"), py::arg("input"));
+  act.def("gelu_new", &gelu_new, "GELU implementation used in GPT-2.", py::arg("out"),
+          py::arg("input"));
+  act.def("gelu_fast", &gelu_fast, "Approximate GELU implementation.", py::arg("out"),
+          py::arg("input"));
+
+  auto moe = m.def_submodule("moe_ops");
+  moe.def("topk_softmax", &topk_softmax, "Apply topk softmax to the gating outputs.",
+          py::arg("topk_weights"), py::arg("topk_indices"), py::arg("token_expert_indices"),
+          py::arg("gating_output"), py::arg("renormalize") = false);
+  moe.def("moe_align_block_size", &moe_align_block_size,
+          "Aligning the number of tokens to be processed by each expert such that it is "
+          "divisible by the block size.",
+          py::arg("topk_ids"), py::arg("num_experts"), py::arg("block_size"),
+          py::arg("sorted_token_ids"), py::arg("experts_ids"), py::arg("num_tokens_post_pad"),
+          py::arg("fill_padding") = false);
+
+  auto kv = m.def_submodule("kv_transfer_ops");
+  kv.def("copy_blocks_p2p", &copy_blocks_p2p,
+         "Copy KV blocks src_block_ids of src_caches onto dst_block_ids of dst_caches "
+         "(per-layer caches, possibly on different GPUs; pull on the destination GPU by default).",
+         py::arg("src_caches"), py::arg("dst_caches"), py::arg("src_block_ids"),
+         py::arg("dst_block_ids"), py::arg("method") = 0, py::arg("push") = false,
+         py::arg("bad_pairs") = py::none());
+  kv.def("copy_blocks_from_ptrs", &copy_blocks_from_ptrs, py::arg("src_ptrs"),
+         py::arg("src_num_blocks"), py::arg("dst_caches"), py::arg("src_block_ids"),
+         py::arg("dst_block_ids"), py::arg("method") = 0, py::arg("bad_pairs") = py::none());
+  kv.def("copy_blocks_to_ptrs", &copy_blocks_to_ptrs, py::arg("src_caches"), py::arg("dst_ptrs"),
+         py::arg("dst_num_blocks"), py::arg("src_block_ids"), py::arg("dst_block_ids"),
+         py::arg("method") = 0, py::arg("bad_pairs") = py::none());
+  kv.def("gather_blocks", &gather_blocks, py::arg("caches"), py::arg("block_ids"), py::arg("out"),
+         py::arg("bad_ids") = py::none());
+  kv.def("scatter_blocks", &scatter_blocks, py::arg("src"), py::arg("caches"),
+         py::arg("block_ids"), py::arg("bad_ids") = py::none());
+  kv.def("ipc_get_handle", &ipc_get_handle, py::arg("tensor"));
+  kv.def("ipc_open_handle", &ipc_open_handle, py::arg("handle"), py::arg("device"));
+  kv.def("ipc_close_handle", &ipc_close_handle, py::arg("base"));
+  kv.def("enable_peer_access", &enable_peer_access, py::arg("device"), py::arg("peer"));
+  kv.def("can_access_peer", &can_access_peer, py::arg("device"), py::arg("peer"));
+}

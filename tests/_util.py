@@ -1,0 +1,63 @@
+"""Shared helpers for the tests (not a test module)."""
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+# Parity rule for float ops: max|got - ref| / max(max|ref|, 1e-6) <= REL_TOL
+# against the fp32 reference formula (bf16/fp16 outputs).
+REL_TOL = 1e-2
+
+
+def rel_err(got: torch.Tensor, ref: torch.Tensor) -> float:
+    got = got.float().cpu()
+    ref = ref.float().cpu()
+    if ref.numel() == 0:
+        return 0.0
+    return ((got - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()
+
+
+def max_ulps(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype) -> float:
+    """Largest difference in units of the storage type's epsilon at the reference's magnitude."""
+    got = got.float().cpu()
+    ref = ref.float().cpu()
+    if ref.numel() == 0:
+        return 0.0
+    ulp = torch.finfo(dtype).eps * ref.abs().clamp_min(torch.finfo(dtype).tiny)
+    return ((got - ref).abs() / ulp).max().item()
+
+
+def assert_matches_rounded(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype,
+                           min_equal: float = 0.98) -> None:
+    """`ref` reproduces the kernel's rounding points on the CPU.  CPU and GPU
+    exp/tanh/erf may differ in the last fp32 ulp, which can flip a bf16/fp16
+    rounding, so require: almost all elements bit-equal, the rest close.
+    fp32 outputs: within 8 fp32 ulps."""
+    if dtype == torch.float32:
+        assert max_ulps(got, ref, dtype) <= 8.0
+        return
+    g, r = got.float().cpu(), ref.float().cpu()
+    if r.numel() == 0:
+        return
+    frac = (g == r).float().mean().item()
+    assert frac >= min_equal, f"only {frac:.4f} of elements bit-equal"
+    assert rel_err(g, r) <= 1e-3
+
+
+_REF_CACHE = {}
+
+
+def ref_ops(name: str):
+    """The reference's own CUDA module from oracle/_ref, or None if not built."""
+    if name not in _REF_CACHE:
+        try:
+            from oracle.build_ref import load_ref_ops
+
+            _REF_CACHE[name] = load_ref_ops(name)
+        except Exception:
+            _REF_CACHE[name] = None
+    return _REF_CACHE[name]

@@ -1,0 +1,81 @@
+"""CPU: the torch shim keeps the reference's module names and call signatures
+and rejects what it cannot run with RuntimeError, before any GPU work."""
+import inspect
+import re
+
+import pytest
+import torch
+
+import paceserve_b200
+from paceserve_b200 import activation_ops, kv_transfer_ops, layernorm_ops, moe_ops, pos_encoding_ops
+
+# name -> positional parameters of the reference binding (csrc/*.cpp)
+REFERENCE_SIGNATURES = {
+    (layernorm_ops, "rms_norm"): ["out", "input", "weight", "epsilon"],
+    (pos_encoding_ops, "rotary_embedding"): ["positions", "query", "key", "head_size",
+                                             "cos_sin_cache", "is_neox"],
+    (activation_ops, "silu_and_mul"): ["out", "input"],
+    (activation_ops, "gelu_new"): ["out", "input"],
+    (activation_ops, "gelu_fast"): ["out", "input"],
+    (moe_ops, "topk_softmax"): ["topk_weights", "topk_indices", "token_expert_indices",
+                                "gating_output"],
+    (moe_ops, "moe_align_block_size"): ["topk_ids", "num_experts", "block_size",
+                                        "sorted_token_ids", "experts_ids", "num_tokens_post_pad"],
+}
+
+
+def _params(fn):
+    sig = fn.__doc__.splitlines()[0]
+    inner = sig[sig.index("(") + 1: sig.rindex(")")]
+    return [re.split(r"[:=]", p)[0].strip() for p in inner.split(",") if p.strip()]
+
+
+@pytest.mark.parametrize("mod,name", list(REFERENCE_SIGNATURES), ids=lambda x: getattr(x, "__name__", x))
+def test_reference_signatures_preserved(mod, name):
+    got = _params(getattr(mod, name))
+    want = REFERENCE_SIGNATURES[(mod, name)]
+    assert got[: len(want)] == want
+
+
+def test_new_ops_present():
+    assert _params(layernorm_ops.fused_add_rms_norm) == ["input", "residual", "weight", "epsilon"]
+    assert _params(activation_ops.gelu_and_mul) == ["out", "input"]
+    assert _params(activation_ops.gelu_tanh_and_mul) == ["out", "input"]
+    assert _params(kv_transfer_ops.copy_blocks_p2p)[:4] == ["src_caches", "dst_caches",
+                                                            "src_block_ids", "dst_block_ids"]
+
+
+def test_cpu_tensors_rejected():
+    x = torch.randn(4, 16)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        layernorm_ops.rms_norm(torch.empty_like(x), x, torch.ones(16), 1e-5)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        layernorm_ops.fused_add_rms_norm(x, x.clone(), torch.ones(16), 1e-5)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        activation_ops.silu_and_mul(torch.empty(4, 8), x)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        moe_ops.topk_softmax(torch.empty(4, 2), torch.empty(4, 2, dtype=torch.int32),
+                             torch.empty(4, 2, dtype=torch.int32), torch.randn(4, 8))
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        moe_ops.moe_align_block_size(torch.zeros(8, dtype=torch.int32), 8, 64,
+                                     torch.empty(600, dtype=torch.int32),
+                                     torch.empty(10, dtype=torch.int32),
+                                     torch.empty(1, dtype=torch.int32))
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        pos_encoding_ops.rotary_embedding(torch.zeros(4, dtype=torch.long), torch.randn(4, 256),
+                                          torch.randn(4, 128), 128, torch.randn(16, 128), True)
+    with pytest.raises(RuntimeError, match="CUDA tensors on one device"):
+        kv_transfer_ops.copy_blocks_p2p([torch.zeros(2, 16)], [torch.zeros(2, 16)],
+                                        torch.zeros(1, dtype=torch.int32),
+                                        torch.zeros(1, dtype=torch.int32))
+
+
+def test_install_as_paceserve_registers_modules():
+    import sys
+
+    paceserve_b200.install_as_paceserve()
+    from paceserve import layernorm_ops as ln  # noqa: F401  (the reference's import form)
+
+    assert sys.modules["paceserve.layernorm_ops"] is layernorm_ops
+    assert sys.modules["paceserve.moe_ops"] is moe_ops
+    assert inspect.ismodule(sys.modules["paceserve.activation_ops"])
