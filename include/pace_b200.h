@@ -4,7 +4,9 @@
  *
  * Every entry point takes plain device pointers, element counts and strides,
  * a dtype code and a cudaStream_t, launches on that stream, never allocates
- * device memory, never synchronises, and returns a PACE_* status code.  On a
+ * device memory, never synchronises, and returns a PACE_* status code.  The
+ * stream must belong to the calling thread's current device (the launch goes
+ * to that device).  Launches may be captured into a CUDA graph.  On a
  * non-zero status, pace_last_error() returns a message for the calling thread.
  * Row strides are in ELEMENTS of the row's dtype.
  *
@@ -153,7 +155,7 @@ int pace_moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel
  * src_layers / dst_layers are HOST arrays of num_layers device pointers (each
  * may be a peer device's memory, reachable after pace_enable_peer_access or
  * through pace_ipc_open_handle); the two id arrays are DEVICE int32 arrays.
- * The kernel runs on the stream's device: the destination's device pulls over
+ * The kernel runs on the current device (the stream's): the destination's device pulls over
  * NVLink, the source's device pushes.  Pairs with an id outside
  * [0, src_num_blocks) / [0, dst_num_blocks) are skipped and counted into
  * *bad_pairs (device int32, may be NULL; the caller zeroes it).  Destination

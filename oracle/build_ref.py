@@ -81,6 +81,10 @@ def build(ref_root: str = "/root/reference", verbose: bool = False, jobs: int = 
     if not os.path.isdir(os.path.join(ref_root, "csrc")):
         return []
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
+    # a host compiler that links libstdc++ dynamically (a static copy inside
+    # an extension breaks c10's std::ostream-based error messages)
+    if os.path.exists("/usr/bin/g++"):
+        os.environ["CXX"] = "/usr/bin/g++"
     os.environ.setdefault("MAX_JOBS", "4")
     with ThreadPoolExecutor(max_workers=jobs) as ex:
         futs = [ex.submit(_build_one, n, ref_root, verbose) for n in REF_MODULES]

@@ -1,0 +1,106 @@
+"""Time the reference's own CUDA ops (built from its sources into oracle/_ref)
+against this package's kernels on the bench's op chain, on one B200.
+
+TEST / MEASUREMENT INFRASTRUCTURE ONLY: it runs the reference as a
+comparison point and never feeds the product.
+
+The reference chain is what PaceServe runs today (models/llama.py:232-255):
+rms_norm, rotary_embedding with the cache in the model dtype (the reference
+requires it, rotary_embedding.py:53), a PyTorch residual add followed by
+rms_norm where this package has fused_add_rms_norm, and silu_and_mul.
+Each op is also timed alone (a CUDA graph of its 32 launches over the 32
+layers' distinct buffers, so every launch reads cold data).
+
+Usage (GPU box): python oracle/compare_ref_cuda.py [--out file.json]
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+from oracle.build_ref import load_ref_ops  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=None)
+    ap.add_argument("--reps", type=int, default=50)
+    args = ap.parse_args()
+    import paceserve_b200 as pb
+
+    dev = torch.device("cuda:0")
+    ln_r, pe_r, act_r = (load_ref_ops(n) for n in ("layernorm_ops", "pos_encoding_ops", "activation_ops"))
+    if None in (ln_r, pe_r, act_r):
+        raise SystemExit("reference ops not built")
+    ch = bench.build_chain(dev, seed=7)
+    H, HD, EPS = bench.H, bench.HD, bench.EPS
+    cache_bf16 = ch["cache"].to(torch.bfloat16)
+    lay = ch["layers"]
+    pos = ch["positions"]
+    for b in lay:
+        b.setdefault("normed", torch.empty(bench.T, H, dtype=torch.bfloat16, device=dev))
+        b["res_sum"] = torch.empty(bench.T, H, dtype=torch.bfloat16, device=dev)
+
+    def ref_chain():
+        for l, b in enumerate(lay):
+            if l == 0:
+                ln_r.rms_norm(b["normed"], b["hidden"], b["w_in"], EPS)
+            else:  # residual + hidden, then RMSNorm (llama.py:248-252)
+                torch.add(b["hidden"], b["residual"], out=b["res_sum"])
+                ln_r.rms_norm(b["normed"], b["res_sum"], b["w_in"], EPS)
+            pe_r.rotary_embedding(pos, b["q"], b["k"], HD, cache_bf16, True)
+            torch.add(b["attn"], b["residual2"], out=b["res_sum"])
+            ln_r.rms_norm(b["normed"], b["res_sum"], b["w_post"], EPS)
+            act_r.silu_and_mul(b["act"], b["gate_up"])
+
+    ours = (pb.layernorm_ops, pb.pos_encoding_ops, pb.activation_ops)
+    res = {}
+    for name, fn in (("ours", lambda: bench.run_chain(ch, ours)), ("reference_cuda", ref_chain)):
+        g = bench.capture(fn)
+        ms = bench.time_replays(g, args.reps, 5) / args.reps
+        res[name] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(bench.T / (ms * 1e-3), 1)}
+        del g
+    single = {
+        "rms_norm": (lambda: [ln_r.rms_norm(b["normed"], b["hidden"], b["w_in"], EPS) for b in lay],
+                     lambda: [pb.layernorm_ops.rms_norm(b["normed"], b["hidden"], b["w_in"], EPS) for b in lay],
+                     bench.B_RMS),
+        "rotary_embedding": (lambda: [pe_r.rotary_embedding(pos, b["q"], b["k"], HD, cache_bf16, True) for b in lay],
+                             lambda: [pb.pos_encoding_ops.rotary_embedding(pos, b["q"], b["k"], HD, ch["cache"], True)
+                                      for b in lay],
+                             bench.B_ROPE),
+        "silu_and_mul": (lambda: [act_r.silu_and_mul(b["act"], b["gate_up"]) for b in lay],
+                         lambda: [pb.activation_ops.silu_and_mul(b["act"], b["gate_up"]) for b in lay],
+                         bench.B_SILU),
+        "add+rms_norm vs fused_add_rms_norm": (
+            lambda: [(torch.add(b["attn"], b["residual2"], out=b["res_sum"]),
+                      ln_r.rms_norm(b["normed"], b["res_sum"], b["w_post"], EPS)) for b in lay],
+            lambda: [pb.layernorm_ops.fused_add_rms_norm(b["attn"], b["residual2"], b["w_post"], EPS) for b in lay],
+            bench.B_FUSED),
+    }
+    per_op = {}
+    for name, (rf, of, nbytes) in single.items():
+        row = {}
+        for who, fn in (("reference_cuda", rf), ("ours", of)):
+            g = bench.capture(fn)
+            us = bench.time_replays(g, args.reps, 3) * 1e3 / (args.reps * bench.L)
+            row[who] = {"us_per_launch": round(us, 3), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+            del g
+        row["speedup"] = round(row["reference_cuda"]["us_per_launch"] / row["ours"]["us_per_launch"], 2)
+        per_op[name] = row
+    res["per_op"] = per_op
+    res["chain_speedup"] = round(res["reference_cuda"]["ms_per_step"] / res["ours"]["ms_per_step"], 2)
+    line = json.dumps(res)
+    print(line)
+    if args.out:
+        with open(args.out, "w") as f:
+            f.write(line + "\n")
+
+
+if __name__ == "__main__":
+    main()

@@ -27,7 +27,7 @@ try:
 except ImportError as exc:  # pragma: no cover - exercised only on a broken install
     raise ImportError(
         "paceserve_b200: the native extension is not built "
-        f"({exc}); run `python -m paceserve_b200.build`"
+        f"({exc}); run `python paceserve_b200/build.py`"
     ) from exc
 
 layernorm_ops = _C.layernorm_ops

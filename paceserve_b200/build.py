@@ -8,7 +8,9 @@ Outputs, next to this file:
     the C ABI; it links ``libpace_b200.so`` through ``$ORIGIN``.
 
 Objects go to ``<repo>/_build``.  Steps whose outputs are newer than every
-input are skipped.  Run ``python -m paceserve_b200.build`` (or ``build()``).
+input are skipped.  Run ``python paceserve_b200/build.py`` (or
+``__graft_entry__.build()``); the package itself cannot be imported before
+the extension exists.
 """
 from __future__ import annotations
 
@@ -29,7 +31,8 @@ EXT = os.path.join(PKG, "_C.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH + [
+CCBIN = ["-ccbin", "/usr/bin/g++"] if os.path.exists("/usr/bin/g++") else []
+NVCC_FLAGS = ARCH + CCBIN + [
     "-O3",
     "-std=c++17",
     "-lineinfo",
@@ -62,6 +65,25 @@ def _run(cmd: list[str], verbose: bool) -> None:
         raise RuntimeError(f"build step failed ({r.returncode}): {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
 
 
+def host_cxx() -> str:
+    """A C++ compiler that links libstdc++ as a shared library.  A private static
+    copy inside the extension would meet torch's shared copy in the same
+    std::ostream (c10 error messages) and crash on an uninitialised locale."""
+    for cand in ("/usr/bin/g++", os.environ.get("CXX", ""), "g++"):
+        if not cand or (os.path.isabs(cand) and not os.path.exists(cand)):
+            continue
+        probe = subprocess.run([cand, "-print-file-name=libstdc++.so"], capture_output=True, text=True)
+        if probe.returncode == 0 and os.path.isabs(probe.stdout.strip()):
+            return cand
+    raise RuntimeError("no C++ compiler with a shared libstdc++ found")
+
+
+def check_dynamic_libstdcxx(so: str) -> None:
+    out = subprocess.run(["readelf", "-d", so], capture_output=True, text=True).stdout
+    if "libstdc++.so" not in out:
+        raise RuntimeError(f"{so} does not link libstdc++ dynamically")
+
+
 def _headers() -> list[str]:
     return glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
 
@@ -80,7 +102,8 @@ def build_library(verbose: bool = False, jobs: int = 6) -> str:
     with ThreadPoolExecutor(max_workers=jobs) as ex:
         list(ex.map(lambda c: _run(c, verbose), todo))
     if not _newer(LIB, objs):
-        _run([NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs, verbose)
+        _run([NVCC] + ARCH + CCBIN + ["-shared", "-cudart", "static", "-o", LIB] + objs, verbose)
+        check_dynamic_libstdcxx(LIB)
     return LIB
 
 
@@ -96,7 +119,7 @@ def build_extension(verbose: bool = False) -> str:
     incs = cpp_extension.include_paths(device_type="cuda")
     py_inc = sysconfig.get_paths()["include"]
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
-    cxx = os.environ.get("CXX", "g++")
+    cxx = host_cxx()
     cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", src, "-o", EXT]
     cmd += ["-I" + INCLUDE, "-I" + py_inc] + ["-isystem" + i for i in incs]
     cmd += [
@@ -116,6 +139,7 @@ def build_extension(verbose: bool = False) -> str:
         "-ltorch_python",
     ]
     _run(cmd, verbose)
+    check_dynamic_libstdcxx(EXT)
     return EXT
 
 

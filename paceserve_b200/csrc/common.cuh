@@ -23,26 +23,18 @@ bool pdl_enabled();
 // Number of SMs of `device`, cached.
 int sm_count(int device);
 
-// Makes the stream's device current for the lifetime of the guard.  The
-// legacy / per-thread default streams keep the current device.
+// The device the entry point launches on: the calling thread's current
+// device, which must own the stream (as for any CUDA launch).  No query is
+// made on the stream itself: querying a stream that is being captured into a
+// CUDA graph invalidates the capture.
 class StreamDeviceGuard {
  public:
-  explicit StreamDeviceGuard(cudaStream_t stream) {
-    cudaGetDevice(&prev_);
-    dev_ = prev_;
-    if (stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread) {
-      int d = -1;
-      if (cudaStreamGetDevice(stream, &d) == cudaSuccess && d >= 0) dev_ = d;
-    }
-    if (dev_ != prev_) cudaSetDevice(dev_);
-  }
-  ~StreamDeviceGuard() {
-    if (dev_ != prev_) cudaSetDevice(prev_);
+  explicit StreamDeviceGuard(cudaStream_t) {
+    if (cudaGetDevice(&dev_) != cudaSuccess) dev_ = 0;
   }
   int device() const { return dev_; }
 
  private:
-  int prev_ = 0;
   int dev_ = 0;
 };
 

@@ -33,19 +33,22 @@ def max_ulps(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype) -> float:
 
 def assert_matches_rounded(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype,
                            min_equal: float = 0.98) -> None:
-    """`ref` reproduces the kernel's rounding points on the CPU.  CPU and GPU
-    exp/tanh/erf may differ in the last fp32 ulp, which can flip a bf16/fp16
-    rounding, so require: almost all elements bit-equal, the rest close.
-    fp32 outputs: within 8 fp32 ulps."""
+    """`ref` reproduces the kernel's rounding points (on the CPU, or the
+    reference's own kernel).  exp/tanh/erf implementations may differ in the
+    last fp32 ulps, which can flip a bf16/fp16 rounding, so require: almost
+    all elements bit-equal, the rest within two storage-type ulps at the
+    output's largest magnitude.  fp32 outputs: within 1e-5 of the largest
+    magnitude (tanh-based formulas cancel near 1 + tanh(x) = 0, so per-element
+    ulps can be large)."""
     if dtype == torch.float32:
-        assert max_ulps(got, ref, dtype) <= 8.0
+        assert rel_err(got, ref) <= 1e-5
         return
     g, r = got.float().cpu(), ref.float().cpu()
     if r.numel() == 0:
         return
     frac = (g == r).float().mean().item()
     assert frac >= min_equal, f"only {frac:.4f} of elements bit-equal"
-    assert rel_err(g, r) <= 1e-3
+    assert rel_err(g, r) <= 2 * torch.finfo(dtype).eps
 
 
 _REF_CACHE = {}

@@ -7,7 +7,7 @@ import torch
 
 from oracle import ops_ref
 from paceserve_b200 import activation_ops, cabi, layernorm_ops, pos_encoding_ops
-from tests._util import REL_TOL, assert_matches_rounded, max_ulps, ref_ops, rel_err
+from tests._util import REL_TOL, assert_matches_rounded, ref_ops, rel_err
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
