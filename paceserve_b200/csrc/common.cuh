@@ -76,6 +76,24 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 #endif
 }
 
+// Asks the bulk-copy engine to pull [p, p + bytes) into L2 (p 16-byte aligned,
+// bytes a multiple of 16).  Kernels issue it for their input rows BEFORE
+// pdl_wait(): L2 is the point of coherence, so a line fetched early and then
+// written by the still-running predecessor holds the predecessor's data when
+// this kernel reads it after the wait.  The DRAM latency of the first touch
+// then overlaps the predecessor's tail instead of following it.
+__device__ __forceinline__ void prefetch_l2(const void* p, int64_t bytes) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
+  const char* c = static_cast<const char*>(p);
+  while (bytes > 0) {
+    const uint32_t n = bytes > 32768 ? 32768u : static_cast<uint32_t>(bytes);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
+    c += n;
+    bytes -= n;
+  }
+#endif
+}
+
 // 16-byte global accesses.  *_nc: read-only path for inputs that the kernel
 // does not write; L1::no_allocate keeps single-use streams out of L1.
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {

@@ -48,18 +48,24 @@ __global__ void __launch_bounds__(kMaxThreads)
   using Tr = Traits<T>;
   constexpr int V = Tr::kVec;
   __shared__ float red[32];
-  pdl_launch_dependents();
-  pdl_wait();
-
   const int64_t row = blockIdx.x;
   const int nvec = hidden / V;
   const T* xr = x_in + row * in_stride;
   T* orow = x_out + row * out_stride;
   T* rr = FUSED ? res + row * res_stride : nullptr;
 
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    prefetch_l2(xr, (int64_t)hidden * sizeof(T));
+    if (FUSED) prefetch_l2(rr, (int64_t)hidden * sizeof(T));
+    if (row < 4) prefetch_l2(weight, (int64_t)hidden * sizeof(T));
+  }
+  pdl_wait();
+
   float v[NV][V];
   uint4 raw[NV];
   uint4 rraw[NV];
+  uint4 wraw[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int c = threadIdx.x + j * blockDim.x;
@@ -70,6 +76,7 @@ __global__ void __launch_bounds__(kMaxThreads)
       } else {
         raw[j] = ld_nc_v4(xr + (int64_t)c * V);
       }
+      wraw[j] = __ldg(reinterpret_cast<const uint4*>(weight) + c);
     }
   }
   float ss = 0.f;
@@ -96,7 +103,7 @@ __global__ void __launch_bounds__(kMaxThreads)
     const int c = threadIdx.x + j * blockDim.x;
     if (c < nvec) {
       float w[V];
-      Tr::unpack(__ldg(reinterpret_cast<const uint4*>(weight) + c), w);
+      Tr::unpack(wraw[j], w);
       float o[V];
 #pragma unroll
       for (int e = 0; e < V; ++e) o[e] = Tr::round(v[j][e] * inv) * w[e];

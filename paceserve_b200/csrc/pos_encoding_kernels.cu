@@ -56,9 +56,14 @@ __global__ void __launch_bounds__(512)
                     const C* __restrict__ cache, int rot_dim, int64_t max_position) {
   using Tr = Traits<T>;
   constexpr int V = Tr::kVec;
-  pdl_launch_dependents();
-  pdl_wait();
   const int64_t tok = blockIdx.x;
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    prefetch_l2(query + tok * q_stride, (int64_t)num_heads * head_size * sizeof(T));
+    if (num_kv_heads > 0)
+      prefetch_l2(key + tok * k_stride, (int64_t)num_kv_heads * head_size * sizeof(T));
+  }
+  pdl_wait();
   const int64_t pos = positions[tok];
   if (pos < 0 || pos >= max_position) return;
   const int embed = rot_dim / 2;
