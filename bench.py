@@ -157,12 +157,12 @@ def make_positions(gen, device):
     return torch.cat([pre, dec]).to(device)
 
 
-def rope_cache(device):
-    """cos/sin cache [MAX_POS, HD] in fp32: [cos | sin] of pos * theta^(-2i/HD)."""
+def rope_cache(device, max_pos: int = MAX_POS):
+    """cos/sin cache [max_pos, HD] in fp32: [cos | sin] of pos * theta^(-2i/HD)."""
     import torch
 
     inv = 1.0 / (THETA ** (torch.arange(0, HD, 2, dtype=torch.float64) / HD))
-    t = torch.arange(MAX_POS, dtype=torch.float64)
+    t = torch.arange(max_pos, dtype=torch.float64)
     f = torch.outer(t, inv)
     return torch.cat([f.cos(), f.sin()], -1).float().to(device)
 
@@ -351,6 +351,257 @@ def cpu_chain_sample(budget_s: float = 8.0, max_passes: int = 1 << 30, warmup: i
                       f"{n} layer>=1 passes ({t_sum:.1f} s), scaled to 32 layers"}
 
 
+# ------------------------------------------------------------ KV promotion --
+KV_NB, KV_L, KV_SLAB = 8192, 32, (2, 16, 8, 128)
+KV_BLOCK_BYTES = 2 * 16 * 8 * 128 * 2
+KV_METHODS = {1: "simt", 2: "bulk"}
+
+
+def kv_requests(seed: int):
+    """8 promoted requests, prompt lengths
+    min(8192, round(lognormal(6.9, 0.7))) -> ceil(len/16) blocks each, taken from
+    random occupied blocks of an 80 %-full LP cache and scattered into random free
+    blocks of an HP cache that is 80 % full with other requests."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    lens = np.clip(np.round(rng.lognormal(6.9, 0.7, 8)), 1, 8192).astype(np.int64)
+    blocks = int(((lens + 15) // 16).sum())
+    occupied = rng.permutation(KV_NB)[: int(0.8 * KV_NB)]
+    free = rng.permutation(KV_NB)[int(0.8 * KV_NB):]
+    blocks = min(blocks, len(free))
+    src = rng.choice(occupied, blocks, replace=False)
+    dst = rng.choice(free, blocks, replace=False)
+    return lens, src, dst
+
+
+def _kv_caches(dev, fill_seed=None):
+    import torch
+
+    if fill_seed is None:
+        return [torch.zeros(KV_NB, *KV_SLAB, dtype=torch.bfloat16, device=dev) for _ in range(KV_L)]
+    g = torch.Generator(device=dev).manual_seed(fill_seed)
+    return [torch.randn(KV_NB, *KV_SLAB, generator=g, device=dev).to(torch.bfloat16)
+            for _ in range(KV_L)]
+
+
+def _time_copy(fn, steps, warmup):
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def kv_reference_path(src_caches, dst_caches, src, dst, dev):
+    """The reference mechanism (KVhelper GPU->CPU gather, CPU->GPU index-put), one pass."""
+    import torch
+
+    from oracle import kv_ref
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    host = kv_ref.get_kv_cache(src_caches, src.tolist())
+    t1 = time.perf_counter()
+    kv_ref.insert_kv_cache(dst_caches, host, dst.tolist(), dev)
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1
+
+
+def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
+    """LP->HP promotion on rank pairs (0->1, 2->3, ...): the HP rank pulls the
+    request blocks from the LP rank's caches (CUDA IPC) with one kernel.  With one
+    GPU, LP and HP caches both live on it (an HBM-to-HBM copy).  Returns the
+    result dict on every rank (collectives are taken by all ranks in the same order)."""
+    import torch
+
+    from paceserve_b200 import kv_transfer as kvt
+
+    dev = torch.device(f"cuda:{local}")
+    out = {"workload": "LP->HP KV promotion, Llama-3-8B paged cache [8192, 2, 16, 8, 128] bf16 x 32 "
+                       "layers, 8 requests lognormal(6.9, 0.7) capped 8192, 80 % occupied"}
+    if ws == 1:
+        lens, src, dst = kv_requests(7)
+        sc = _kv_caches(dev, fill_seed=100)
+        dc = _kv_caches(dev)
+        sids = torch.tensor(src, dtype=torch.int32, device=dev)
+        dids = torch.tensor(dst, dtype=torch.int32, device=dev)
+        nbytes = len(src) * KV_L * KV_BLOCK_BYTES
+        res = {}
+        for m, name in KV_METHODS.items():
+            ms = _time_copy(lambda: kvt.promote(sc, dc, sids, dids, method=m), steps, warmup)
+            res[name] = {"ms": round(ms, 4), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                         "hbm_gbs": round(2 * nbytes / (ms * 1e-3) / 1e9, 1)}
+        ok = all(torch.equal(dc[l][dids.long()], sc[l][sids.long()]) for l in range(KV_L))
+        out.update({"mode": "one GPU: HBM -> HBM", "blocks": int(len(src)), "bytes": nbytes,
+                    "byte_exact": bool(ok), "methods": res})
+        if baseline:
+            d2h, h2d = kv_reference_path(sc, dc, src, dst, dev)
+            out["reference_path"] = {"gbs": round(nbytes / (d2h + h2d) / 1e9, 2),
+                                     "d2h_s": round(d2h, 4), "h2d_s": round(h2d, 4),
+                                     "kind": "port", "sample": "KVhelper get_kv_cache/insert_kv_cache "
+                                     "restated (per-layer fancy-index gather to host, index-put back), "
+                                     "one pass, without the Ray object-store hop"}
+        return out
+
+    import torch.distributed as dist
+
+    pairs = kvt.pair_ranks(ws)
+    mine = next(((i, lp, hp) for i, (lp, hp) in enumerate(pairs) if rank in (lp, hp)), None)
+    role = None if mine is None else ("lp" if rank == mine[1] else "hp")
+    caches = None
+    if role == "lp":
+        caches = _kv_caches(dev, fill_seed=100 + mine[0])
+    elif role == "hp":
+        caches = _kv_caches(dev)
+    exports = kvt.exchange_exports(kvt.export_caches(caches) if role == "lp" else None)
+    times = {m: 0.0 for m in KV_METHODS}
+    nbytes, nblocks, imported = 0, 0, None
+    if mine is not None:
+        lens, src, dst = kv_requests(7 + mine[0])
+        nblocks = len(src)
+        nbytes = nblocks * KV_L * KV_BLOCK_BYTES
+    dist.barrier()
+    if role == "hp":
+        imported = kvt.ImportedCaches(exports[mine[1]], local)
+        sids = torch.tensor(src, dtype=torch.int32, device=dev)
+        dids = torch.tensor(dst, dtype=torch.int32, device=dev)
+        for m in KV_METHODS:
+            times[m] = _time_copy(lambda: kvt.promote(imported, caches, sids, dids, method=m),
+                                  steps, warmup)
+    t = torch.tensor([times[m] for m in KV_METHODS], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ok = True
+    if role == "lp":
+        g = torch.stack([c[torch.tensor(src, device=dev)] for c in caches])
+        dist.send(g, dst=mine[2])
+        del g
+    elif role == "hp":
+        g = torch.empty(KV_L, nblocks, *KV_SLAB, dtype=torch.bfloat16, device=dev)
+        dist.recv(g, src=mine[1])
+        ok = bool(torch.equal(torch.stack([c[dids.long()] for c in caches]), g))
+        del g
+        imported.close()
+    info = [None] * ws
+    dist.all_gather_object(info, (role, ok, nbytes))
+    dist.barrier()
+    total = sum(x[2] for x in info if x[0] == "hp")
+    res = {}
+    for i, (m, name) in enumerate(KV_METHODS.items()):
+        ms = t[i].item()
+        res[name] = {"ms_max_over_pairs": round(ms, 4),
+                     "gbs_per_pair": round(total / len(pairs) / (ms * 1e-3) / 1e9, 1),
+                     "aggregate_gbs": round(total / (ms * 1e-3) / 1e9, 1)}
+    best = max(res.values(), key=lambda r: r["gbs_per_pair"])
+    out.update({"mode": f"{len(pairs)} LP->HP pairs over NVLink (pull on the HP GPU, CUDA IPC)",
+                "pairs": len(pairs), "bytes_per_pair_avg": total // max(1, len(pairs)),
+                "byte_exact": all(x[1] for x in info), "methods": res,
+                "nvlink_frac": round(best["gbs_per_pair"] / NVLINK_GBS, 4),
+                "nvlink_peak_gbs": NVLINK_GBS, "nvlink_peak_source": "measured peer copy on this pool"})
+    return out
+
+
+NVLINK_GBS = 770.0  # measured peer copy per direction on this pool (900 nominal)
+
+
+# ------------------------------------------------------------ sweep / MoE --
+def sweep(dev, reps=10):
+    """per-op GB/s for T in {1..16384}, Llama-3-8B and -70B shapes,
+    bf16 and fp16.  Each op is timed as a CUDA graph over enough distinct buffers
+    that every launch reads cold data (working set >= 512 MB per cycle)."""
+    import torch
+
+    import paceserve_b200 as pb
+
+    shapes = {"llama3-8b": (4096, 14336, 32, 8), "llama3-70b": (8192, 28672, 64, 8)}
+    out = []
+    for sname, (h, inter, nq, nkv) in shapes.items():
+        for dtype in (torch.bfloat16, torch.float16):
+            for t in (1, 16, 128, 512, 2048, 8192, 16384):
+                per = {"rms_norm": 4 * h * t + 2 * h, "fused_add_rms_norm": 8 * h * t + 2 * h,
+                       "rotary_embedding": 4 * (nq + nkv) * HD * t + t * HD * 4 + 8 * t,
+                       "silu_and_mul": 6 * inter * t}
+                row = {"shape": sname, "dtype": str(dtype).split(".")[1], "T": t}
+                for op, nbytes in per.items():
+                    nbuf = int(min(32, max(2, -(-512 * 2**20 // nbytes))))
+                    g_ = torch.Generator(device=dev).manual_seed(t)
+                    rn = lambda *sh: torch.randn(*sh, generator=g_, device=dev).to(dtype)  # noqa: E731
+                    if op == "rms_norm":
+                        bufs = [(rn(t, h), torch.empty(t, h, dtype=dtype, device=dev), rn(h)) for _ in range(nbuf)]
+                        fn = lambda: [pb.layernorm_ops.rms_norm(o, x, w, EPS) for x, o, w in bufs]  # noqa: E731
+                    elif op == "fused_add_rms_norm":
+                        bufs = [(rn(t, h), rn(t, h), rn(h)) for _ in range(nbuf)]
+                        fn = lambda: [pb.layernorm_ops.fused_add_rms_norm(x, r, w, EPS) for x, r, w in bufs]  # noqa: E731
+                    elif op == "rotary_embedding":
+                        cache = rope_cache(dev, max(MAX_POS, t))  # every position in range
+                        pos = torch.randint(0, t, (t,), device=dev)
+                        bufs = [rn(t, (nq + 2 * nkv) * HD) for _ in range(nbuf)]
+                        fn = lambda: [pb.pos_encoding_ops.rotary_embedding(  # noqa: E731
+                            pos, q[:, : nq * HD], q[:, nq * HD: (nq + nkv) * HD], HD, cache, True) for q in bufs]
+                    else:
+                        bufs = [(rn(t, 2 * inter), torch.empty(t, inter, dtype=dtype, device=dev)) for _ in range(nbuf)]
+                        fn = lambda: [pb.activation_ops.silu_and_mul(o, x) for x, o in bufs]  # noqa: E731
+                    g = capture(fn)
+                    us = time_replays(g, reps, 3) * 1e3 / (reps * nbuf)
+                    row[op] = {"us": round(us, 3), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+                    del g, bufs
+                out.append(row)
+                torch.cuda.empty_cache()
+    return out
+
+
+def moe_routing(dev, reps=50):
+    """topk_softmax (E=8, top-2, renormalised) then
+    moe_align_block_size (block 64) on N(0,1) fp32 gating logits."""
+    import numpy as np
+    import torch
+
+    import paceserve_b200 as pb
+    from oracle import moe_ref
+
+    out = []
+    for t in (64, 512, 4096, 16384):
+        E, k, bs = 8, 2, 64
+        gating = torch.randn(t, E, generator=torch.Generator().manual_seed(t)).to(dev)
+        w = torch.empty(t, k, device=dev)
+        ids = torch.empty(t, k, dtype=torch.int32, device=dev)
+        tei = torch.empty(t, k, dtype=torch.int32, device=dev)
+        cap = t * k + E * (bs - 1)
+        sorted_ids = torch.empty(cap, dtype=torch.int32, device=dev)
+        expert_ids = torch.empty((cap + bs - 1) // bs, dtype=torch.int32, device=dev)
+        total = torch.empty(1, dtype=torch.int32, device=dev)
+        topk = lambda: pb.moe_ops.topk_softmax(w, ids, tei, gating, True)  # noqa: E731
+        align = lambda: pb.moe_ops.moe_align_block_size(ids, E, bs, sorted_ids, expert_ids, total, True)  # noqa: E731
+        res = {"T": t}
+        for name, fn, nbytes in (("topk_softmax", topk, t * (4 * E + 12 * k)),
+                                 ("moe_align_block_size", align,
+                                  4 * t * k + 4 * cap + 4 * ((cap + bs - 1) // bs) + 4)):
+            g = capture(lambda: [fn() for _ in range(reps)])
+            us = time_replays(g, 5, 3) * 1e3 / (5 * reps)
+            res[name] = {"us": round(us, 3), "gbs": round(nbytes / (us * 1e-6) / 1e9, 2)}
+            del g
+        topk()
+        align()
+        torch.cuda.synchronize()
+        ow, oi, ot = moe_ref.topk_softmax(gating.cpu().numpy(), k, renormalize=True)
+        os_, oe, otot = moe_ref.moe_align_block_size(oi, E, bs)
+        n = int(total.item())
+        res["bit_exact"] = bool(np.array_equal(ids.cpu().numpy(), oi) and n == otot
+                                and np.array_equal(sorted_ids.cpu().numpy(), os_)
+                                and np.array_equal(expert_ids.cpu().numpy()[: n // bs], oe))
+        out.append(res)
+    return out
+
+
 # ------------------------------------------------------------------ main --
 def init_dist():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
@@ -387,6 +638,29 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_side_workload(args, ws, rank, local):
+    import torch
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    if args.workload == "kv":
+        res = kv_promotion(ws, rank, local, steps=min(args.steps, 50), warmup=args.warmup,
+                           baseline=not args.no_cpu_baseline)
+        line = {"metric": "LP->HP KV-promotion GB/s", "n_gpus": ws, "kv_promotion": res}
+    elif args.workload == "sweep":
+        line = {"metric": "per-op HBM GB/s, token sweep", "sweep": sweep(dev) if rank == 0 else None,
+                "peak_gbs": peaks()["hbm_gbs"]}
+    else:
+        line = {"metric": "MoE routing us/op", "moe": moe_routing(dev) if rank == 0 else None}
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -394,9 +668,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["chain", "kv", "sweep", "moe"], default="chain",
+                    help="chain: the driver's line (config 2); kv: LP->HP promotion (config 5); "
+                         "sweep: per-op token sweep (config 3); moe: routing (config 4)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = init_dist()
+    if args.impl == "ours" and args.workload != "chain":
+        run_side_workload(args, ws, rank, local)
+        return
     if args.impl == "reference":
         run_reference(args, ws, rank)
         if ws > 1:
@@ -459,6 +739,12 @@ def main():
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_chain_sample()
     if ws > 1:
+        del ch
+        torch.cuda.empty_cache()
+        try:
+            line["kv_promotion"] = kv_promotion(ws, rank, local, steps=min(args.steps, 20), warmup=3)
+        except Exception as exc:  # reported, never fatal for the chain line
+            line["kv_promotion"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
