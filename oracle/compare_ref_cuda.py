@@ -94,6 +94,37 @@ def main():
         row["speedup"] = round(row["reference_cuda"]["us_per_launch"] / row["ours"]["us_per_launch"], 2)
         per_op[name] = row
     res["per_op"] = per_op
+    # MoE routing (config 4): the reference wrapper pre-fills sorted_ids with
+    # torch (fused_moe.py:191-195) before its moe_align_block_size; ours fills
+    # the padding in the kernel.
+    moe_r = load_ref_ops("moe_ops")
+    moe = []
+    for t in (64, 512, 4096, 16384):
+        E, k, bs = 8, 2, 64
+        gating = torch.randn(t, E, generator=torch.Generator().manual_seed(t)).to(dev)
+        w = torch.empty(t, k, device=dev)
+        ids = torch.empty(t, k, dtype=torch.int32, device=dev)
+        tei = torch.empty(t, k, dtype=torch.int32, device=dev)
+        cap = t * k + E * (bs - 1)
+        srt = torch.empty(cap, dtype=torch.int32, device=dev)
+        eid = torch.empty((cap + bs - 1) // bs, dtype=torch.int32, device=dev)
+        tot = torch.empty(1, dtype=torch.int32, device=dev)
+        cases = {
+            "reference_cuda": (lambda: moe_r.topk_softmax(w, ids, tei, gating),
+                               lambda: (srt.fill_(t * k), moe_r.moe_align_block_size(ids, E, bs, srt, eid, tot))),
+            "ours": (lambda: pb.moe_ops.topk_softmax(w, ids, tei, gating, False),
+                     lambda: pb.moe_ops.moe_align_block_size(ids, E, bs, srt, eid, tot, True)),
+        }
+        row = {"T": t}
+        for who, (tk, al) in cases.items():
+            r = {}
+            for name, fn in (("topk_softmax", tk), ("moe_align_block_size", al)):
+                g = bench.capture(lambda: [fn() for _ in range(20)])
+                r[name + "_us"] = round(bench.time_replays(g, 5, 3) * 1e3 / 100, 3)
+                del g
+            row[who] = r
+        moe.append(row)
+    res["moe"] = moe
     res["chain_speedup"] = round(res["reference_cuda"]["ms_per_step"] / res["ours"]["ms_per_step"], 2)
     line = json.dumps(res)
     print(line)

@@ -17,12 +17,15 @@
 // moe_align_block_size (reference csrc/moe_align_block_size_kernels.cu:23-109).
 // Output semantics: per-expert counts padded to a multiple of block_size,
 // expert_ids per block, and sorted_token_ids holding, for each expert, its flat
-// indices in ASCENDING order.  Design: one CTA of up to 32 warps; each warp owns
-// a contiguous slice of the flat index range; counting uses warp match-any
-// aggregation into per-warp shared counters, a shared-memory scan gives every
-// (warp, expert) its start, and a second pass scatters with the rank inside
-// each 32-wide group from the match mask -- a stable counting sort with no
-// global scratch and no atomics on global memory.
+// indices in ASCENDING order.  Design: one CTA of up to 32 warps; the expert ids
+// are staged once into shared memory as int16 (vector loads, all in flight
+// together) when they fit; each warp owns a contiguous slice of the flat index
+// range.  For E <= 32 a warp counts and ranks each 32-entry group with one
+// ballot per expert (lane x keeps expert x's count and next slot in a
+// register); larger E use shared-memory atomics and match-any.  A
+// shared-memory scan gives every (warp, expert) its start, and the second pass
+// scatters by rank within the group -- a stable counting sort with no global
+// scratch and no global atomics.
 #include "common.cuh"
 
 namespace pace {
@@ -236,21 +239,68 @@ __device__ __forceinline__ int load_expert(const I* ids, int64_t i, int num_expe
   return (e >= 0 && e < num_experts) ? (int)e : -1;
 }
 
-__device__ __forceinline__ int upper_bound_excl(const int* cum, int n, int v) {
-  // largest e in [0, n) with cum[e] <= v (cum is non-decreasing, cum[0] = 0)
-  int lo = 0, hi = n - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (cum[mid] <= v)
-      lo = mid;
-    else
-      hi = mid - 1;
-  }
-  return lo;
+// Number of 4-byte words before the staged expert ids in shared memory:
+// cnt[NW][E] | cum[E+1] | tot[E] | scan[32], rounded up to 8 bytes.
+__host__ __device__ inline int64_t moe_align_words(int nw, int num_experts) {
+  const int64_t w = (int64_t)nw * num_experts + 2LL * num_experts + 1 + 32;
+  return (w + 1) & ~1LL;
 }
 
-// Shared layout: cnt[NW][E] | cum[E+1] | tot[E] | scan[32]
+// Expert of every flat entry as int16 in shared memory (-1 for ids outside
+// [0, E)), read with all loads of a thread issued before its stores: 16-byte
+// vectors for 4-byte ids on a 16-byte boundary, 8 scalar loads in flight
+// otherwise.
 template <typename I>
+__device__ __forceinline__ void stage_experts(const I* __restrict__ ids, int64_t numel, int E,
+                                              int16_t* ex) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  if constexpr (sizeof(I) == 4) {
+    if ((reinterpret_cast<uintptr_t>(ids) & 15u) == 0) {
+      const int64_t nv = numel / 4;
+      const int4* v4 = reinterpret_cast<const int4*>(ids);
+      for (int64_t base = tid; base < nv; base += (int64_t)nt * 4) {
+        int4 r[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t v = base + (int64_t)k * nt;
+          if (v < nv) r[k] = __ldg(v4 + v);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t v = base + (int64_t)k * nt;
+          if (v < nv) {
+            const int q[4] = {r[k].x, r[k].y, r[k].z, r[k].w};
+            short4 o;
+            o.x = (short)((q[0] >= 0 && q[0] < E) ? q[0] : -1);
+            o.y = (short)((q[1] >= 0 && q[1] < E) ? q[1] : -1);
+            o.z = (short)((q[2] >= 0 && q[2] < E) ? q[2] : -1);
+            o.w = (short)((q[3] >= 0 && q[3] < E) ? q[3] : -1);
+            *reinterpret_cast<short4*>(ex + 4 * v) = o;
+          }
+        }
+      }
+      for (int64_t i = nv * 4 + tid; i < numel; i += nt) ex[i] = (int16_t)load_expert(ids, i, E);
+      return;
+    }
+  }
+  for (int64_t base = tid; base < numel; base += (int64_t)nt * 8) {
+    int v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t i = base + (int64_t)k * nt;
+      v[k] = i < numel ? load_expert(ids, i, E) : -1;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t i = base + (int64_t)k * nt;
+      if (i < numel) ex[i] = (int16_t)v[k];
+    }
+  }
+}
+
+// STAGED: the expert ids are first copied into shared memory (when they fit),
+// so the two counting passes never wait on global memory inside their loops.
+template <typename I, bool STAGED>
 __global__ void __launch_bounds__(1024)
     moe_align_kernel(const I* __restrict__ ids, int64_t numel, int num_experts, int block_size,
                      int32_t* __restrict__ sorted_ids, int64_t sorted_capacity,
@@ -263,10 +313,12 @@ __global__ void __launch_bounds__(1024)
   int* cum = cnt + NW * E;
   int* tot = cum + E + 1;
   int* scan = tot + E;
+  int16_t* ex = reinterpret_cast<int16_t*>(smem + moe_align_words(NW, E));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_launch_dependents();
   pdl_wait();
 
+  if (STAGED) stage_experts(ids, numel, E, ex);
   for (int i = tid; i < NW * E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
 
@@ -276,16 +328,24 @@ __global__ void __launch_bounds__(1024)
   int* wcnt = cnt + warp * E;
   const unsigned lt_mask = (1u << lane) - 1u;
 
-  // Pass 1: per-warp counts.
-  for (int64_t base = begin; base < end; base += 32) {
-    const int64_t i = base + lane;
-    const int e = i < end ? load_expert(ids, i, E) : -1;
-    const unsigned active = __ballot_sync(0xffffffffu, e >= 0);
-    if (e >= 0) {
-      const unsigned peers = __match_any_sync(active, e);
-      if ((peers & lt_mask) == 0) wcnt[e] += __popc(peers);
+  // Pass 1: per-warp counts.  E <= 32: one ballot per expert per 32 entries,
+  // lane x accumulating expert x; otherwise shared-memory atomics.
+  if (E <= 32) {
+    int c = 0;
+    for (int64_t base = begin; base < end; base += 32) {
+      const int64_t i = base + lane;
+      const int e = i < end ? (STAGED ? (int)ex[i] : load_expert(ids, i, E)) : -1;
+      for (int x = 0; x < E; ++x) {
+        const unsigned b = __ballot_sync(0xffffffffu, e == x);
+        if (lane == x) c += __popc(b);
+      }
     }
-    __syncwarp();
+    if (lane < E) wcnt[lane] = c;
+  } else {
+    for (int64_t i = begin + lane; i < end; i += 32) {
+      const int e = STAGED ? (int)ex[i] : load_expert(ids, i, E);
+      if (e >= 0) atomicAdd(&wcnt[e], 1);
+    }
   }
   __syncthreads();
 
@@ -335,32 +395,186 @@ __global__ void __launch_bounds__(1024)
 
   const int total = cum[E];
   if (tid == 0) *total_post_pad = total;
-  for (int b = tid; b < total / block_size; b += blockDim.x)
-    expert_ids[b] = upper_bound_excl(cum, E + 1, b * block_size);
-  if (fill_padding) {
-    for (int64_t p = tid; p < sorted_capacity; p += blockDim.x) {
-      bool pad = p >= total;
-      if (!pad) {
-        const int e = upper_bound_excl(cum, E + 1, (int)p);
-        pad = (int)p - cum[e] >= tot[e];
+  // Each expert's blocks and padding slots, one warp per expert.
+  for (int e = warp; e < E; e += NW) {
+    for (int b = cum[e] / block_size + lane; b < cum[e + 1] / block_size; b += 32) expert_ids[b] = e;
+    if (fill_padding)
+      for (int p = cum[e] + tot[e] + lane; p < cum[e + 1]; p += 32) sorted_ids[p] = (int32_t)numel;
+  }
+  if (fill_padding)
+    for (int64_t p = total + tid; p < sorted_capacity; p += blockDim.x) sorted_ids[p] = (int32_t)numel;
+
+  // Pass 2: stable scatter; an entry's slot is its expert's next free slot in
+  // this warp's range plus its rank among the group's lanes with that expert.
+  if (E <= 32) {
+    int next = lane < E ? cum[lane] + wcnt[lane] : 0;  // lane x: next slot of expert x
+    for (int64_t base = begin; base < end; base += 32) {
+      const int64_t i = base + lane;
+      const int e = i < end ? (STAGED ? (int)ex[i] : load_expert(ids, i, E)) : -1;
+      unsigned peers = 0;
+      int grown = 0;
+      for (int x = 0; x < E; ++x) {
+        const unsigned b = __ballot_sync(0xffffffffu, e == x);
+        if (e == x) peers = b;
+        if (lane == x) grown = __popc(b);
       }
-      if (pad) sorted_ids[p] = (int32_t)numel;
+      const int slot = __shfl_sync(0xffffffffu, next, e >= 0 ? e : 0);
+      if (e >= 0) sorted_ids[slot + __popc(peers & lt_mask)] = (int32_t)i;
+      next += grown;
+    }
+  } else {
+    for (int64_t base = begin; base < end; base += 32) {
+      const int64_t i = base + lane;
+      const int e = i < end ? (STAGED ? (int)ex[i] : load_expert(ids, i, E)) : -1;
+      const unsigned active = __ballot_sync(0xffffffffu, e >= 0);
+      unsigned peers = 0;
+      if (e >= 0) {
+        peers = __match_any_sync(active, e);
+        sorted_ids[cum[e] + wcnt[e] + __popc(peers & lt_mask)] = (int32_t)i;
+      }
+      __syncwarp();
+      if (e >= 0 && (peers & lt_mask) == 0) wcnt[e] += __popc(peers);
+      __syncwarp();
     }
   }
+}
 
-  // Pass 2: stable scatter.
-  for (int64_t base = begin; base < end; base += 32) {
-    const int64_t i = base + lane;
-    const int e = i < end ? load_expert(ids, i, E) : -1;
-    const unsigned active = __ballot_sync(0xffffffffu, e >= 0);
-    unsigned peers = 0;
-    if (e >= 0) {
-      peers = __match_any_sync(active, e);
-      sorted_ids[cum[e] + wcnt[e] + __popc(peers & lt_mask)] = (int32_t)i;
+// ---------------------------------------------- cluster version, E <= 32 --
+// For large inputs the counting sort is spread over a thread-block cluster of
+// G <= 8 CTAs (one per SM): CTA r stages and counts the r-th slice, the
+// per-CTA expert totals are exchanged through distributed shared memory
+// across a cluster barrier, and every CTA then scatters its own slice.  No
+// global scratch is used.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// Address of `p` (this CTA's shared memory) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(out)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ int ld_cluster(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+constexpr int kClusterMax = 8;  // portable cluster size
+constexpr int kClusterWarps = 16;
+
+// Shared layout (ints): cnt[NW][32] | ctot[32] | base[32] | tot[32] | cum[33] (+pad) | ex[int16]
+template <typename I>
+__global__ void __launch_bounds__(kClusterWarps * 32)
+    moe_align_cluster_kernel(const I* __restrict__ ids, int64_t numel, int num_experts,
+                             int block_size, int32_t* __restrict__ sorted_ids,
+                             int64_t sorted_capacity, int32_t* __restrict__ expert_ids,
+                             int32_t* __restrict__ total_post_pad, int fill_padding,
+                             int64_t slice) {
+  extern __shared__ int smem[];
+  const int E = num_experts;
+  const int NW = blockDim.x >> 5;
+  int* cnt = smem;               // [NW][32]: per-warp counts, then exclusive prefixes
+  int* ctot = cnt + NW * 32;     // this CTA's totals (read by the other CTAs)
+  int* base = ctot + 32;         // entries of each expert in earlier CTAs
+  int* tot = base + 32;          // cluster-wide totals
+  int* cum = tot + 32;           // padded exclusive cumsum [E+1]
+  int16_t* ex = reinterpret_cast<int16_t*>(cum + 34);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t rank = cluster_rank();
+  const int G = gridDim.x;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  const int64_t s0 = (int64_t)rank * slice;
+  const int64_t s1 = s0 + slice < numel ? s0 + slice : numel;
+  const int64_t n = s1 > s0 ? s1 - s0 : 0;
+  stage_experts(ids + s0, n, E, ex);
+  __syncthreads();
+
+  const int64_t chunk = ceil_div(ceil_div(n, NW), 32) * 32;
+  const int64_t begin = (int64_t)warp * chunk;
+  const int64_t end = begin + chunk < n ? begin + chunk : n;
+  int c = 0;
+  for (int64_t b = begin; b < end; b += 32) {
+    const int64_t i = b + lane;
+    const int e = i < end ? (int)ex[i] : -1;
+    for (int x = 0; x < E; ++x) {
+      const unsigned m = __ballot_sync(0xffffffffu, e == x);
+      if (lane == x) c += __popc(m);
     }
-    __syncwarp();
-    if (e >= 0 && (peers & lt_mask) == 0) wcnt[e] += __popc(peers);
-    __syncwarp();
+  }
+  cnt[warp * 32 + lane] = c;
+  __syncthreads();
+  if (tid < 32) {
+    int run = 0;
+    for (int w = 0; w < NW; ++w) {
+      const int v = cnt[w * 32 + tid];
+      cnt[w * 32 + tid] = run;
+      run += v;
+    }
+    ctot[tid] = run;
+  }
+  cluster_sync_all();  // every CTA's ctot is complete and visible
+  if (tid < 32) {
+    int t = 0, bs = 0;
+    for (int r = 0; r < G; ++r) {
+      const int v = ld_cluster(cluster_addr(&ctot[tid], (uint32_t)r));
+      t += v;
+      if (r < (int)rank) bs += v;
+    }
+    tot[tid] = t;
+    base[tid] = bs;
+  }
+  cluster_sync_all();  // no CTA leaves while another may still read its ctot
+  if (warp == 0) {
+    const int padded = lane < E ? (tot[lane] + block_size - 1) / block_size * block_size : 0;
+    int incl = padded;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    cum[lane] = incl - padded;
+    if (lane == 31) cum[32] = incl;
+  }
+  __syncthreads();
+  const int total = cum[32];
+  if (rank == 0 && tid == 0) *total_post_pad = total;
+  const int gw = (int)rank * NW + warp;
+  for (int e = gw; e < E; e += G * NW) {
+    for (int b = cum[e] / block_size + lane; b < cum[e + 1] / block_size; b += 32) expert_ids[b] = e;
+    if (fill_padding)
+      for (int p = cum[e] + tot[e] + lane; p < cum[e + 1]; p += 32) sorted_ids[p] = (int32_t)numel;
+  }
+  if (fill_padding)
+    for (int64_t p = total + (int64_t)rank * blockDim.x + tid; p < sorted_capacity;
+         p += (int64_t)G * blockDim.x)
+      sorted_ids[p] = (int32_t)numel;
+
+  int next = lane < E ? cum[lane] + base[lane] + cnt[warp * 32 + lane] : 0;
+  for (int64_t b = begin; b < end; b += 32) {
+    const int64_t i = b + lane;
+    const int e = i < end ? (int)ex[i] : -1;
+    unsigned peers = 0;
+    int grown = 0;
+    for (int x = 0; x < E; ++x) {
+      const unsigned m = __ballot_sync(0xffffffffu, e == x);
+      if (e == x) peers = m;
+      if (lane == x) grown = __popc(m);
+    }
+    const int slot = __shfl_sync(0xffffffffu, next, e >= 0 ? e : 0);
+    if (e >= 0) sorted_ids[slot + __popc(peers & lt_mask)] = (int32_t)(s0 + i);
+    next += grown;
   }
 }
 
@@ -448,22 +662,75 @@ extern "C" int pace_moe_align_block_size(const void* topk_ids, int ids_dtype, in
                 (long long)expert_ids_capacity, (long long)ceil_div(need, block_size));
   if (!sorted_token_ids || !expert_ids || !num_tokens_post_pad || (numel > 0 && !topk_ids))
     return fail(PACE_ERR_INVALID_ARGUMENT, "moe_align_block_size: null pointer");
-  // Warps: enough that each owns >= 256 entries, at most 32, and the per-warp
-  // counters fit in shared memory.
-  int nw = (int)ceil_div(numel, 256);
-  if (nw < 1) nw = 1;
+  StreamDeviceGuard guard(stream);
+  // Inputs above 2048 entries with E <= 32: a cluster of up to 8 CTAs, >= 1024
+  // entries each.
+  if (numel > 2048 && num_experts <= 32) {
+    int g = (int)ceil_div(numel, 1024);
+    if (g > kClusterMax) g = kClusterMax;
+    const int64_t slice = ceil_div(ceil_div(numel, g), 32) * 32;
+    const int64_t csmem = (kClusterWarps * 32 + 32 * 3 + 34) * 4 + ((slice * 2 + 7) & ~7LL);
+    if (csmem <= 200 * 1024) {
+      auto run_cluster = [&](auto type_tag) -> int {
+        using I = decltype(type_tag);
+        auto kern = moe_align_cluster_kernel<I>;
+        cudaError_t e = cudaSuccess;
+        if (csmem > 48 * 1024)
+          e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_align_block_size: cluster attributes");
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(g);
+        cfg.blockDim = dim3(kClusterWarps * 32);
+        cfg.dynamicSmemBytes = (size_t)csmem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = g;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.numAttrs = 1;
+        if (pdl_enabled()) {
+          attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+          attr[1].val.programmaticStreamSerializationAllowed = 1;
+          cfg.numAttrs = 2;
+        }
+        cfg.attrs = attr;
+        e = cudaLaunchKernelEx(&cfg, kern, static_cast<const I*>(topk_ids), numel, num_experts,
+                               block_size, sorted_token_ids, sorted_capacity, expert_ids,
+                               num_tokens_post_pad, fill_padding, slice);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_align_block_size (cluster)");
+        return PACE_OK;
+      };
+      switch (ids_dtype) {
+        case PACE_U8: return run_cluster(uint8_t{});
+        case PACE_I8: return run_cluster(int8_t{});
+        case PACE_I16: return run_cluster(int16_t{});
+        case PACE_I32: return run_cluster(int32_t{});
+        case PACE_I64: return run_cluster(int64_t{});
+        default:
+          return fail(PACE_ERR_UNSUPPORTED_DTYPE,
+                      "moe_align_block_size: unsupported ids dtype %d", ids_dtype);
+      }
+    }
+  }
+  // One CTA: 4 to 32 warps, each owning >= 64 entries when there are enough
+  // (>= 256 above 2048 entries), and per-warp counters that fit in shared memory.
+  int nw = (int)ceil_div(numel, numel > 2048 ? 256 : 64);
+  if (nw < 4) nw = 4;
   if (nw > 32) nw = 32;
-  const int64_t fixed_ints = 2LL * num_experts + 1 + 32;
   const int64_t max_smem = 200 * 1024;
-  while (nw > 1 && (nw * (int64_t)num_experts + fixed_ints) * 4 > max_smem) nw >>= 1;
-  const int64_t smem = (nw * (int64_t)num_experts + fixed_ints) * 4;
-  if (smem > max_smem)
+  while (nw > 1 && moe_align_words(nw, num_experts) * 4 > max_smem) nw >>= 1;
+  const int64_t counters = moe_align_words(nw, num_experts) * 4;
+  // Stage the ids in shared memory as int16 when they fit next to the counters.
+  const int64_t staged_bytes = counters + ((numel * 2 + 7) & ~7LL);
+  const bool staged = num_experts <= 32767 && staged_bytes <= max_smem;
+  const int64_t smem = staged ? staged_bytes : counters;
+  if (counters > max_smem)
     return fail(PACE_ERR_TOO_LARGE, "moe_align_block_size: num_experts=%d too large",
                 num_experts);
-  StreamDeviceGuard guard(stream);
   auto run = [&](auto type_tag) -> int {
     using I = decltype(type_tag);
-    auto kern = moe_align_kernel<I>;
+    auto kern = staged ? moe_align_kernel<I, true> : moe_align_kernel<I, false>;
     if (smem > 48 * 1024) {
       cudaError_t e =
           cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

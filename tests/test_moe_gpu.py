@@ -145,6 +145,21 @@ def test_moe_align_block_size(numel, E, bs, dtype):
         np.testing.assert_array_equal(re_.cpu().numpy()[: t // bs], e[: t // bs])
 
 
+@pytest.mark.parametrize("numel,E,bs", [(4097, 1, 16), (20000, 32, 64), (65536, 8, 64),
+                                        (6000, 3, 7), (131072, 16, 128)])
+@pytest.mark.parametrize("fill", [False, True])
+def test_moe_align_large_inputs(numel, E, bs, fill):
+    """The multi-CTA (thread-block cluster) path, with ids outside [0, E) mixed in."""
+    rng = np.random.default_rng(numel + 7 * E)
+    ids = rng.integers(-1, E + 1, size=numel)
+    t_ids = torch.from_numpy(ids).to(torch.int32)
+    s, e, t = run_align(t_ids, E, bs, fill_padding=fill, prefill=None if not fill else -3)
+    os_, oe, ot = moe_ref.moe_align_block_size_c(ids, E, bs)
+    assert t == ot
+    np.testing.assert_array_equal(s, os_)
+    np.testing.assert_array_equal(e[: t // bs], oe)
+
+
 def test_moe_align_fill_padding_and_invalid_ids():
     ids = torch.tensor([0, 9, 1, -1, 1, 3, 3, 3], dtype=torch.int64)
     s, e, t = run_align(ids, 4, 2, fill_padding=True, prefill=-5)
