@@ -188,6 +188,43 @@ int pace_kv_scatter_blocks(const void* in, void* const* layers, int num_layers,
                            const int32_t* block_ids, int64_t n, int64_t block_bytes,
                            int64_t num_blocks, int32_t* bad_ids, cudaStream_t stream);
 
+/* ---- paged-KV append -----------------------------------------------------
+ * Write nnz new tokens' K and V rows ([kv_heads * head_dim] each, row strides
+ * in elements: the k/v views of a fused qkv tensor) into the paged cache
+ * [num_pages, 2, page_size, kv_heads, head_dim] (K at index 0, V at 1).  Token
+ * i belongs to request b = batch_indices[i] at sequence position
+ * p = positions[i] and lands on page kv_indices[kv_indptr[b] + p / page_size],
+ * slot p % page_size.  kv_indptr has batch_size + 1 entries, kv_indices
+ * num_kv_indices; a request's length is (pages - 1) * page_size +
+ * kv_last_page_len[b].  Tokens whose request, position or page is out of range
+ * are skipped and counted into *bad_tokens (device int32, may be NULL).
+ * Replaces flashinfer.page.append_paged_kv_cache (FlashInfer 0.2.0, pinned in
+ * PaceServe's requirements.txt:40), called at
+ * paceserve/model_executor/attention/flashinfer_attention_wrapper.py:245-255. */
+int pace_append_paged_kv_cache(const void* key, const void* value, int64_t nnz,
+                               int num_kv_heads, int head_dim, int64_t key_row_stride,
+                               int64_t value_row_stride, const int32_t* batch_indices,
+                               const int32_t* positions, void* paged_cache, int64_t num_pages,
+                               int page_size, const int32_t* kv_indices, int64_t num_kv_indices,
+                               const int32_t* kv_indptr, const int32_t* kv_last_page_len,
+                               int64_t batch_size, int32_t* bad_tokens, int dtype,
+                               cudaStream_t stream);
+
+/* Same, with each token's request and position derived in the kernel from
+ * append_indptr [batch_size + 1]: request b's tokens are the last
+ * append_indptr[b+1] - append_indptr[b] tokens of its sequence.  Replaces
+ * the get_seq_lens + get_batch_indices_positions + append_paged_kv_cache
+ * sequence at flashinfer_attention_wrapper.py:239-255 with one launch. */
+int pace_append_paged_kv_cache_by_indptr(const void* key, const void* value, int64_t nnz,
+                                         int num_kv_heads, int head_dim,
+                                         int64_t key_row_stride, int64_t value_row_stride,
+                                         const int32_t* append_indptr, void* paged_cache,
+                                         int64_t num_pages, int page_size,
+                                         const int32_t* kv_indices, int64_t num_kv_indices,
+                                         const int32_t* kv_indptr,
+                                         const int32_t* kv_last_page_len, int64_t batch_size,
+                                         int32_t* bad_tokens, int dtype, cudaStream_t stream);
+
 /* ---- peer access and CUDA IPC (KV promotion across processes) ----------- */
 #define PACE_IPC_HANDLE_BYTES 64
 /* Make `peer`'s memory addressable from `device` (idempotent).  New: the

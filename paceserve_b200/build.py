@@ -47,6 +47,7 @@ CUDA_SOURCES = [
     "activation_kernels.cu",
     "moe_kernels.cu",
     "kv_transfer_kernels.cu",
+    "kv_append_kernels.cu",
 ]
 
 

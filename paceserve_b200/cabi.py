@@ -66,6 +66,16 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [_P, POINTER(c_void_p), c_int, _P, c_int64, c_int64, c_int64, _P, _P],
     ),
+    "pace_append_paged_kv_cache": (
+        c_int,
+        [_P, _P, c_int64, c_int, c_int, c_int64, c_int64, _P, _P, _P, c_int64, c_int, _P, c_int64,
+         _P, _P, c_int64, _P, c_int, _P],
+    ),
+    "pace_append_paged_kv_cache_by_indptr": (
+        c_int,
+        [_P, _P, c_int64, c_int, c_int, c_int64, c_int64, _P, _P, c_int64, c_int, _P, c_int64, _P,
+         _P, c_int64, _P, c_int, _P],
+    ),
     "pace_enable_peer_access": (c_int, [c_int, c_int]),
     "pace_can_access_peer": (c_int, [c_int, c_int, POINTER(c_int)]),
     "pace_ipc_get_handle": (c_int, [_P, c_void_p, POINTER(c_int64)]),

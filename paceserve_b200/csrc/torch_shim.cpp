@@ -412,6 +412,114 @@ void scatter_blocks(const Tensor& src, const std::vector<Tensor>& caches, const 
                op);
 }
 
+// ------------------------------------------------------- paged-KV append --
+// K or V rows of nnz tokens: [nnz, heads, hd] (heads contiguous) or [nnz, heads*hd].
+int64_t kv_row_stride(const Tensor& t, int64_t heads, int64_t hd, const char* op, const char* name) {
+  TORCH_CHECK(t.is_cuda(), op, ": ", name, " must be a CUDA tensor");
+  if (t.dim() == 3) {
+    TORCH_CHECK(t.size(1) == heads && t.size(2) == hd, op, ": ", name, " must be [nnz, ", heads,
+                ", ", hd, "]");
+    TORCH_CHECK((hd <= 1 || t.stride(2) == 1) && (heads <= 1 || t.stride(1) == hd), op, ": ", name,
+                " heads must be contiguous");
+    return t.size(0) <= 1 ? heads * hd : t.stride(0);
+  }
+  TORCH_CHECK(t.dim() == 2 && t.size(1) == heads * hd, op, ": ", name, " must be [nnz, ",
+              heads * hd, "] or [nnz, ", heads, ", ", hd, "]");
+  TORCH_CHECK(t.size(1) <= 1 || t.stride(1) == 1, op, ": ", name, " rows must be contiguous");
+  return t.size(0) <= 1 ? heads * hd : t.stride(0);
+}
+
+struct PagedCache {
+  int64_t pages, page_size, heads, hd;
+};
+
+PagedCache paged_cache_of(const Tensor& c, const std::string& layout, const char* op) {
+  TORCH_CHECK(layout == "NHD", op, ": only the NHD layout [pages, 2, page_size, kv_heads, head_dim] "
+              "(PaceServe's, flashinfer_attention_wrapper.py:63-73) is supported");
+  TORCH_CHECK(c.is_cuda() && c.dim() == 5 && c.size(1) == 2 && c.is_contiguous(), op,
+              ": paged_kv_cache must be a contiguous CUDA tensor [pages, 2, page_size, kv_heads, "
+              "head_dim]");
+  return {c.size(0), c.size(2), c.size(3), c.size(4)};
+}
+
+Tensor int32_on(const Tensor& t, const Tensor& like, const char* op, const char* name) {
+  TORCH_CHECK(t.device() == like.device(), op, ": ", name, " must be on the cache's device");
+  TORCH_CHECK(t.scalar_type() == at::kInt && t.dim() == 1, op, ": ", name,
+              " must be a 1-D int32 tensor");
+  return t.contiguous();
+}
+
+// flashinfer.page.append_paged_kv_cache's signature (FlashInfer 0.2.0).
+void append_paged_kv_cache(const Tensor& append_key, const Tensor& append_value,
+                           const Tensor& batch_indices, const Tensor& positions,
+                           Tensor& paged_kv_cache, const Tensor& kv_indices,
+                           const Tensor& kv_indptr, const Tensor& kv_last_page_len,
+                           const std::string& kv_layout, const c10::optional<Tensor>& bad_tokens) {
+  const char* op = "append_paged_kv_cache";
+  const PagedCache pc = paged_cache_of(paged_kv_cache, kv_layout, op);
+  TORCH_CHECK(append_key.scalar_type() == paged_kv_cache.scalar_type() &&
+                  append_value.scalar_type() == paged_kv_cache.scalar_type(),
+              op, ": key, value and cache must share a dtype");
+  check_same_device(append_key, paged_kv_cache, op);
+  check_same_device(append_value, paged_kv_cache, op);
+  const int64_t ks = kv_row_stride(append_key, pc.heads, pc.hd, op, "append_key");
+  const int64_t vs = kv_row_stride(append_value, pc.heads, pc.hd, op, "append_value");
+  const int64_t nnz = append_key.size(0);
+  TORCH_CHECK(append_value.size(0) == nnz, op, ": key and value token counts differ");
+  Tensor bi = int32_on(batch_indices, paged_kv_cache, op, "batch_indices");
+  Tensor po = int32_on(positions, paged_kv_cache, op, "positions");
+  Tensor ki = int32_on(kv_indices, paged_kv_cache, op, "kv_indices");
+  Tensor kp = int32_on(kv_indptr, paged_kv_cache, op, "kv_indptr");
+  Tensor kl = int32_on(kv_last_page_len, paged_kv_cache, op, "kv_last_page_len");
+  TORCH_CHECK(bi.numel() >= nnz && po.numel() >= nnz, op,
+              ": batch_indices and positions need one entry per token");
+  TORCH_CHECK(kp.numel() >= 1 && kl.numel() >= kp.numel() - 1, op,
+              ": kv_indptr needs batch + 1 entries and kv_last_page_len batch entries");
+  int32_t* bad = bad_tokens.has_value() ? bad_tokens->data_ptr<int32_t>() : nullptr;
+  const at::cuda::CUDAGuard guard(paged_kv_cache.device());
+  check_status(pace_append_paged_kv_cache(
+                   append_key.data_ptr(), append_value.data_ptr(), nnz, (int)pc.heads, (int)pc.hd,
+                   ks, vs, bi.data_ptr<int32_t>(), po.data_ptr<int32_t>(),
+                   paged_kv_cache.data_ptr(), pc.pages, (int)pc.page_size, ki.data_ptr<int32_t>(),
+                   ki.numel(), kp.data_ptr<int32_t>(), kl.data_ptr<int32_t>(), kp.numel() - 1, bad,
+                   pace_dtype(paged_kv_cache), stream_of(paged_kv_cache)),
+               op);
+}
+
+// One launch for get_seq_lens + get_batch_indices_positions + append.
+void append_paged_kv_cache_by_indptr(const Tensor& append_key, const Tensor& append_value,
+                                     const Tensor& append_indptr, Tensor& paged_kv_cache,
+                                     const Tensor& kv_indices, const Tensor& kv_indptr,
+                                     const Tensor& kv_last_page_len,
+                                     const c10::optional<Tensor>& bad_tokens) {
+  const char* op = "append_paged_kv_cache_by_indptr";
+  const PagedCache pc = paged_cache_of(paged_kv_cache, "NHD", op);
+  TORCH_CHECK(append_key.scalar_type() == paged_kv_cache.scalar_type() &&
+                  append_value.scalar_type() == paged_kv_cache.scalar_type(),
+              op, ": key, value and cache must share a dtype");
+  check_same_device(append_key, paged_kv_cache, op);
+  check_same_device(append_value, paged_kv_cache, op);
+  const int64_t ks = kv_row_stride(append_key, pc.heads, pc.hd, op, "append_key");
+  const int64_t vs = kv_row_stride(append_value, pc.heads, pc.hd, op, "append_value");
+  const int64_t nnz = append_key.size(0);
+  TORCH_CHECK(append_value.size(0) == nnz, op, ": key and value token counts differ");
+  Tensor ai = int32_on(append_indptr, paged_kv_cache, op, "append_indptr");
+  Tensor ki = int32_on(kv_indices, paged_kv_cache, op, "kv_indices");
+  Tensor kp = int32_on(kv_indptr, paged_kv_cache, op, "kv_indptr");
+  Tensor kl = int32_on(kv_last_page_len, paged_kv_cache, op, "kv_last_page_len");
+  TORCH_CHECK(ai.numel() == kp.numel() && kl.numel() >= kp.numel() - 1 && kp.numel() >= 1, op,
+              ": append_indptr and kv_indptr need batch + 1 entries, kv_last_page_len batch");
+  int32_t* bad = bad_tokens.has_value() ? bad_tokens->data_ptr<int32_t>() : nullptr;
+  const at::cuda::CUDAGuard guard(paged_kv_cache.device());
+  check_status(pace_append_paged_kv_cache_by_indptr(
+                   append_key.data_ptr(), append_value.data_ptr(), nnz, (int)pc.heads,
+                   (int)pc.hd, ks, vs, ai.data_ptr<int32_t>(), paged_kv_cache.data_ptr(), pc.pages,
+                   (int)pc.page_size, ki.data_ptr<int32_t>(), ki.numel(), kp.data_ptr<int32_t>(),
+                   kl.data_ptr<int32_t>(), kp.numel() - 1, bad, pace_dtype(paged_kv_cache),
+                   stream_of(paged_kv_cache)),
+               op);
+}
+
 py::tuple ipc_get_handle(const Tensor& t) {
   TORCH_CHECK(t.is_cuda(), "ipc_get_handle: tensor must be on a CUDA device");
   const at::cuda::CUDAGuard guard(t.device());
@@ -506,6 +614,17 @@ PYBIND11_MODULE(_C, m) {
          py::arg("bad_ids") = py::none());
   kv.def("scatter_blocks", &scatter_blocks, py::arg("src"), py::arg("caches"),
          py::arg("block_ids"), py::arg("bad_ids") = py::none());
+  kv.def("append_paged_kv_cache", &append_paged_kv_cache,
+         "Append K/V rows of new tokens to a paged cache (flashinfer.append_paged_kv_cache).",
+         py::arg("append_key"), py::arg("append_value"), py::arg("batch_indices"),
+         py::arg("positions"), py::arg("paged_kv_cache"), py::arg("kv_indices"),
+         py::arg("kv_indptr"), py::arg("kv_last_page_len"), py::arg("kv_layout") = "NHD",
+         py::arg("bad_tokens") = py::none());
+  kv.def("append_paged_kv_cache_by_indptr", &append_paged_kv_cache_by_indptr,
+         "Append, deriving each token's request and position from append_indptr in the kernel.",
+         py::arg("append_key"), py::arg("append_value"), py::arg("append_indptr"),
+         py::arg("paged_kv_cache"), py::arg("kv_indices"), py::arg("kv_indptr"),
+         py::arg("kv_last_page_len"), py::arg("bad_tokens") = py::none());
   kv.def("ipc_get_handle", &ipc_get_handle, py::arg("tensor"));
   kv.def("ipc_open_handle", &ipc_open_handle, py::arg("handle"), py::arg("device"));
   kv.def("ipc_close_handle", &ipc_close_handle, py::arg("base"));

@@ -1,0 +1,125 @@
+"""GPU: paged-KV append (FlashInfer append_paged_kv_cache semantics, as PaceServe
+calls it at flashinfer_attention_wrapper.py:239-255), byte-exact against the
+CPU restatement, for a Sarathi mixed batch built like begin_forward (:75-209)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import append_ref
+from paceserve_b200 import cabi, kv_transfer_ops as kv
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def mixed_batch(rng, page_size=16, num_pages=600, prefills=((448, 0),), decodes=64, max_ctx=2000):
+    """Metadata as begin_forward builds it: prefill chunks first (chunk length,
+    tokens already processed), then decode requests of random context length.
+    Pages are distinct random pages of the cache."""
+    free = list(rng.permutation(num_pages))
+    append_indptr, kv_indptr, kv_indices, last = [0], [0], [], []
+    for chunk, done in prefills:
+        total = done + chunk
+        n_pages = (total + page_size - 1) // page_size
+        kv_indices += [free.pop() for _ in range(n_pages)]
+        append_indptr.append(append_indptr[-1] + chunk)
+        kv_indptr.append(kv_indptr[-1] + n_pages)
+        last.append(total % page_size or page_size)
+    for _ in range(decodes):
+        ctx = int(rng.integers(1, max_ctx))
+        n_pages = (ctx + page_size - 1) // page_size
+        kv_indices += [free.pop() for _ in range(n_pages)]
+        append_indptr.append(append_indptr[-1] + 1)
+        kv_indptr.append(kv_indptr[-1] + n_pages)
+        last.append(ctx % page_size or page_size)
+    t = lambda x: torch.tensor(x, dtype=torch.int32)  # noqa: E731
+    return t(append_indptr), t(kv_indptr), t(kv_indices), t(last)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("form", ["indices", "indptr"])
+def test_append_mixed_batch_matches_oracle(dtype, form):
+    rng = np.random.default_rng(3)
+    nq, nkv, hd, P, ps = 32, 8, 128, 2000, 16
+    ai, kp, ki, kl = mixed_batch(rng, ps, P, prefills=((448, 0), (37, 100)), decodes=64, max_ctx=512)
+    nnz = int(ai[-1])
+    g = torch.Generator().manual_seed(4)
+    qkv = torch.randn(nnz, (nq + 2 * nkv) * hd, generator=g).to(dtype)
+    key, value = qkv[:, nq * hd: (nq + nkv) * hd], qkv[:, (nq + nkv) * hd:]
+    cache = torch.randn(P, 2, ps, nkv, hd, generator=g).to(dtype)
+    seq = append_ref.get_seq_lens(kp, kl, ps)
+    bi, pos = append_ref.get_batch_indices_positions(ai, seq, nnz)
+    ref = append_ref.append_paged_kv_cache(key, value, bi, pos, cache.clone(), ki, kp, kl)
+    got = cache.to(DEV)
+    qd = qkv.to(DEV)
+    kd, vd = qd[:, nq * hd: (nq + nkv) * hd], qd[:, (nq + nkv) * hd:]  # strided views
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    if form == "indices":
+        kv.append_paged_kv_cache(kd, vd, bi.to(DEV), pos.to(DEV), got, ki.to(DEV), kp.to(DEV),
+                                 kl.to(DEV), "NHD", bad)
+    else:
+        kv.append_paged_kv_cache_by_indptr(kd, vd, ai.to(DEV), got, ki.to(DEV), kp.to(DEV),
+                                           kl.to(DEV), bad)
+    torch.cuda.synchronize()
+    assert bad.item() == 0
+    assert torch.equal(got.cpu(), ref)
+
+
+def test_append_3d_rows_decode_only_and_unaligned_heads():
+    rng = np.random.default_rng(5)
+    nkv, hd, P, ps = 2, 36, 1000, 16  # 72-element rows: not a multiple of 16 bytes in bf16 -> scalar path
+    ai, kp, ki, kl = mixed_batch(rng, ps, P, prefills=(), decodes=40, max_ctx=300)
+    nnz = int(ai[-1])
+    key = torch.randn(nnz, nkv, hd).bfloat16()
+    value = torch.randn(nnz, nkv, hd).bfloat16()
+    cache = torch.zeros(P, 2, ps, nkv, hd).bfloat16()
+    bi, pos = append_ref.get_batch_indices_positions(ai, append_ref.get_seq_lens(kp, kl, ps), nnz)
+    ref = append_ref.append_paged_kv_cache(key, value, bi, pos, cache.clone(), ki, kp, kl)
+    got = cache.to(DEV)
+    kv.append_paged_kv_cache_by_indptr(key.to(DEV), value.to(DEV), ai.to(DEV), got, ki.to(DEV),
+                                       kp.to(DEV), kl.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(got.cpu(), ref)
+
+
+def test_append_bad_tokens_skipped_and_counted():
+    nkv, hd, P, ps = 8, 128, 8, 16
+    key = torch.randn(4, nkv * hd, device=DEV).bfloat16()
+    value = torch.randn(4, nkv * hd, device=DEV).bfloat16()
+    cache = torch.zeros(P, 2, ps, nkv, hd, device=DEV).bfloat16()
+    kp = torch.tensor([0, 2], dtype=torch.int32, device=DEV)        # one request, 2 pages
+    kl = torch.tensor([5], dtype=torch.int32, device=DEV)           # length 21
+    ki = torch.tensor([3, 99], dtype=torch.int32, device=DEV)       # second page out of range
+    bi = torch.tensor([0, 0, 1, 0], dtype=torch.int32, device=DEV)  # token 2: no request 1
+    pos = torch.tensor([0, 20, 3, 21], dtype=torch.int32, device=DEV)  # 20 -> page 99; 21 >= length
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kv.append_paged_kv_cache(key, value, bi, pos, cache, ki, kp, kl, "NHD", bad)
+    torch.cuda.synchronize()
+    assert bad.item() == 3
+    assert torch.equal(cache[3, 0, 0], key[0].view(nkv, hd))
+    assert torch.equal(cache[3, 1, 0], value[0].view(nkv, hd))
+    assert int(cache.ne(0).sum()) == 2 * nkv * hd
+    with pytest.raises(RuntimeError, match="NHD"):
+        kv.append_paged_kv_cache(key, value, bi, pos, cache, ki, kp, kl, "HND")
+
+
+def test_append_through_c_abi():
+    lib = cabi.load()
+    rng = np.random.default_rng(9)
+    nkv, hd, P, ps = 8, 128, 200, 16
+    ai, kp, ki, kl = mixed_batch(rng, ps, P, prefills=((20, 30),), decodes=5, max_ctx=100)
+    nnz = int(ai[-1])
+    key = torch.randn(nnz, nkv * hd).bfloat16()
+    value = torch.randn(nnz, nkv * hd).bfloat16()
+    cache = torch.zeros(P, 2, ps, nkv, hd).bfloat16()
+    bi, pos = append_ref.get_batch_indices_positions(ai, append_ref.get_seq_lens(kp, kl, ps), nnz)
+    ref = append_ref.append_paged_kv_cache(key, value, bi, pos, cache.clone(), ki, kp, kl)
+    d = {n: t.to(DEV) for n, t in dict(key=key, value=value, bi=bi, pos=pos, cache=cache, ki=ki,
+                                       kp=kp, kl=kl).items()}
+    st = torch.cuda.current_stream().cuda_stream
+    cabi.check(lib.pace_append_paged_kv_cache(
+        d["key"].data_ptr(), d["value"].data_ptr(), nnz, nkv, hd, nkv * hd, nkv * hd,
+        d["bi"].data_ptr(), d["pos"].data_ptr(), d["cache"].data_ptr(), P, ps, d["ki"].data_ptr(),
+        ki.numel(), d["kp"].data_ptr(), d["kl"].data_ptr(), kp.numel() - 1, None, cabi.PACE_BF16, st))
+    torch.cuda.synchronize()
+    assert torch.equal(d["cache"].cpu(), ref)
