@@ -510,6 +510,55 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
     return out
 
 
+def append_metadata(seed: int = 11, page_size: int = 16, num_pages: int = 4096):
+    """begin_forward's append metadata (flashinfer_attention_wrapper.py:75-209) for the
+    Sarathi batch: one 448-token prefill chunk starting at position 0, then 64
+    decode requests with contexts uniform in [1, 1024]; distinct random pages."""
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng(seed)
+    free = list(rng.permutation(num_pages))
+    ai, kp, ki, kl = [0], [0], [], []
+    lens = [T_PREFILL] + [int(x) for x in rng.integers(1, 1025, T_DECODE)]
+    chunks = [T_PREFILL] + [1] * T_DECODE
+    for n_new, total in zip(chunks, lens):
+        pages = (total + page_size - 1) // page_size
+        ki += [int(free.pop()) for _ in range(pages)]
+        ai.append(ai[-1] + n_new)
+        kp.append(kp[-1] + pages)
+        kl.append(total % page_size or page_size)
+    t = lambda x: torch.tensor(x, dtype=torch.int32)  # noqa: E731
+    return t(ai), t(kp), t(ki), t(kl)
+
+
+def append_bench(dev, reps: int = 20):
+    """Paged-KV append of one step's 512 new K/V tokens into each of the 32
+    layers' caches (graph of 32 launches, distinct caches and qkv buffers)."""
+    import torch
+
+    import paceserve_b200 as pb
+
+    num_pages = 4096
+    ai, kp, ki, kl = (x.to(dev) for x in append_metadata(num_pages=num_pages))
+    g = torch.Generator(device=dev).manual_seed(5)
+    caches = [torch.zeros(num_pages, 2, 16, NKV, HD, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    qkvs = [torch.randn(T, (NQ + 2 * NKV) * HD, generator=g, device=dev).bfloat16() for _ in range(L)]
+    kv = pb.kv_transfer_ops
+
+    def fn():
+        for c, q in zip(caches, qkvs):
+            kv.append_paged_kv_cache_by_indptr(q[:, NQ * HD:(NQ + NKV) * HD], q[:, (NQ + NKV) * HD:],
+                                               ai, c, ki, kp, kl)
+    gr = capture(fn)
+    us = time_replays(gr, reps, 3) * 1e3 / (reps * L)
+    nbytes = 2 * 2 * T * NKV * HD * 2  # read K and V rows, write them into the pages
+    return {"us_per_layer": round(us, 3), "bytes_per_layer": nbytes,
+            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "workload": "append_paged_kv_cache_by_indptr, 448 prefill + 64 decode tokens, "
+                        "8 kv heads x 128, page 16, per layer"}
+
+
 NVLINK_GBS = 770.0  # measured peer copy per direction on this pool (900 nominal)
 
 
@@ -647,6 +696,9 @@ def run_side_workload(args, ws, rank, local):
         res = kv_promotion(ws, rank, local, steps=min(args.steps, 50), warmup=args.warmup,
                            baseline=not args.no_cpu_baseline)
         line = {"metric": "LP->HP KV-promotion GB/s", "n_gpus": ws, "kv_promotion": res}
+        if rank == 0:
+            torch.cuda.empty_cache()
+            line["kv_append"] = append_bench(dev)
     elif args.workload == "sweep":
         line = {"metric": "per-op HBM GB/s, token sweep", "sweep": sweep(dev) if rank == 0 else None,
                 "peak_gbs": peaks()["hbm_gbs"]}

@@ -125,6 +125,57 @@ def main():
             row[who] = r
         moe.append(row)
     res["moe"] = moe
+    # Paged-KV append: FlashInfer's path as PaceServe calls it
+    # (flashinfer_attention_wrapper.py:239-255: get_seq_lens,
+    # get_batch_indices_positions, append_paged_kv_cache) against the one-launch
+    # by-indptr kernel.  The image's FlashInfer builds its page module on first
+    # use; a failure is recorded, not raised.
+    try:
+        import flashinfer
+
+        ai, kp, ki, kl = (x.to(dev) for x in bench.append_metadata())
+        caches = [torch.zeros(4096, 2, 16, bench.NKV, HD, dtype=torch.bfloat16, device=dev)
+                  for _ in range(bench.L)]
+        qkvs = [b["qkv"] for b in lay]
+        NQ, NKV = bench.NQ, bench.NKV
+        nnz = int(ai[-1].item())
+
+        def fi():
+            for c, q in zip(caches, qkvs):
+                k = q[:, NQ * HD:(NQ + NKV) * HD].contiguous().reshape(-1, NKV, HD)
+                v = q[:, (NQ + NKV) * HD:].contiguous().reshape(-1, NKV, HD)
+                sl = flashinfer.get_seq_lens(kp, kl, 16)
+                bi, po = flashinfer.get_batch_indices_positions(ai, sl, nnz)
+                flashinfer.append_paged_kv_cache(k, v, bi, po, c, ki, kp, kl, kv_layout="NHD")
+
+        def mine():
+            for c, q in zip(caches, qkvs):
+                pb.kv_transfer_ops.append_paged_kv_cache_by_indptr(
+                    q[:, NQ * HD:(NQ + NKV) * HD], q[:, (NQ + NKV) * HD:], ai, c, ki, kp, kl)
+        row = {}
+        for who, fn in (("flashinfer_" + flashinfer.__version__, fi), ("ours", mine)):
+            fn()
+            torch.cuda.synchronize()
+            g = bench.capture(fn)
+            row[who + "_us_per_layer"] = round(bench.time_replays(g, 20, 3) * 1e3 / (20 * bench.L), 3)
+            del g
+        ref_c = [c.clone() for c in caches]
+        for c in caches:
+            c.zero_()
+        mine()
+        torch.cuda.synchronize()
+        for c in ref_c:
+            c.zero_()
+        for c, q in zip(ref_c, qkvs):
+            k = q[:, NQ * HD:(NQ + NKV) * HD].contiguous().reshape(-1, NKV, HD)
+            v = q[:, (NQ + NKV) * HD:].contiguous().reshape(-1, NKV, HD)
+            bi, po = flashinfer.get_batch_indices_positions(ai, flashinfer.get_seq_lens(kp, kl, 16), nnz)
+            flashinfer.append_paged_kv_cache(k, v, bi, po, c, ki, kp, kl, kv_layout="NHD")
+        torch.cuda.synchronize()
+        row["byte_equal_to_flashinfer"] = all(torch.equal(a, b) for a, b in zip(caches, ref_c))
+        res["kv_append"] = row
+    except Exception as exc:  # recorded, not fatal
+        res["kv_append"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     res["chain_speedup"] = round(res["reference_cuda"]["ms_per_step"] / res["ours"]["ms_per_step"], 2)
     line = json.dumps(res)
     print(line)

@@ -123,3 +123,34 @@ def test_append_through_c_abi():
         ki.numel(), d["kp"].data_ptr(), d["kl"].data_ptr(), kp.numel() - 1, None, cabi.PACE_BF16, st))
     torch.cuda.synchronize()
     assert torch.equal(d["cache"].cpu(), ref)
+
+
+def test_append_matches_flashinfer_when_available():
+    """Byte-equality with the dependency PaceServe calls (the image's FlashInfer;
+    PaceServe pins 0.2.0), on the bench's mixed-batch metadata."""
+    try:
+        import flashinfer
+    except Exception as exc:  # pragma: no cover
+        pytest.skip(f"flashinfer not importable: {exc}")
+    import bench
+
+    ai, kp, ki, kl = (x.to(DEV) for x in bench.append_metadata())
+    nnz = int(ai[-1].item())
+    nkv, hd = bench.NKV, bench.HD
+    g = torch.Generator(device=DEV).manual_seed(8)
+    k = torch.randn(nnz, nkv, hd, generator=g, device=DEV).bfloat16()
+    v = torch.randn(nnz, nkv, hd, generator=g, device=DEV).bfloat16()
+    a = torch.zeros(4096, 2, 16, nkv, hd, dtype=torch.bfloat16, device=DEV)
+    b = torch.zeros_like(a)
+    try:
+        sl = flashinfer.get_seq_lens(kp, kl, 16)
+        bi, po = flashinfer.get_batch_indices_positions(ai, sl, nnz)
+        flashinfer.append_paged_kv_cache(k, v, bi, po, b, ki, kp, kl, kv_layout="NHD")
+        torch.cuda.synchronize()
+    except Exception as exc:  # pragma: no cover - JIT build unavailable
+        pytest.skip(f"flashinfer page module unavailable: {exc}")
+    kv.append_paged_kv_cache_by_indptr(k, v, ai, a, ki, kp, kl)
+    c = torch.zeros_like(a)
+    kv.append_paged_kv_cache(k, v, bi, po, c, ki, kp, kl)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and torch.equal(c, b)
