@@ -279,8 +279,10 @@ def per_op_times(ch, ops, reps=20):
     return out
 
 
-def e2e_chain(ch, ops, steps, warmup):
-    """Public-API path: pinned host inputs -> device, eager op calls, device -> host output."""
+def e2e_chain(ch, ops, steps, warmup, ws=1):
+    """Public-API path: pinned host inputs -> device, eager op calls, device -> host output.
+    With ws > 1 every rank runs it between barriers; the time is the max over ranks
+    and the value the whole job's tokens/s."""
     import torch
 
     dev = ch["positions"].device
@@ -298,6 +300,11 @@ def e2e_chain(ch, ops, steps, warmup):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize(dev)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        torch.cuda.synchronize(dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -306,7 +313,11 @@ def e2e_chain(ch, ops, steps, warmup):
     e1.record()
     e1.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    return {"value": round(T / (ms * 1e-3), 1), "unit": UNIT,
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return {"value": round(ws * T / (ms * 1e-3), 1), "unit": UNIT,
             "h2d_bytes_per_step": h_pos.numel() * 8 + h_hidden.numel() * 2,
             "d2h_bytes_per_step": h_out.numel() * 2, "ms_per_step": round(ms, 4),
             "steps": steps, "path": "eager calls of paceserve_b200 ops (pybind -> C ABI)"}
@@ -467,7 +478,7 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
     times = {m: 0.0 for m in KV_METHODS}
     nbytes, nblocks, imported = 0, 0, None
     if mine is not None:
-        lens, src, dst = kv_requests(7 + mine[0])
+        lens, src, dst = kv_requests(7)  # the same promotion on every pair
         nblocks = len(src)
         nbytes = nblocks * KV_L * KV_BLOCK_BYTES
     dist.barrier()
@@ -492,14 +503,17 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
         del g
         imported.close()
     info = [None] * ws
-    dist.all_gather_object(info, (role, ok, nbytes))
+    dist.all_gather_object(info, (role, ok, nbytes, [times[m] for m in KV_METHODS]))
     dist.barrier()
-    total = sum(x[2] for x in info if x[0] == "hp")
+    hps = [x for x in info if x[0] == "hp"]
+    total = sum(x[2] for x in hps)
     res = {}
     for i, (m, name) in enumerate(KV_METHODS.items()):
         ms = t[i].item()
+        own = [x[2] / (x[3][i] * 1e-3) / 1e9 for x in hps]  # each pair: its bytes / its time
         res[name] = {"ms_max_over_pairs": round(ms, 4),
                      "gbs_per_pair": round(total / len(pairs) / (ms * 1e-3) / 1e9, 1),
+                     "gbs_per_pair_min_max": [round(min(own), 1), round(max(own), 1)],
                      "aggregate_gbs": round(total / (ms * 1e-3) / 1e9, 1)}
     best = max(res.values(), key=lambda r: r["gbs_per_pair"])
     out.update({"mode": f"{len(pairs)} LP->HP pairs over NVLink (pull on the HP GPU, CUDA IPC)",
@@ -770,7 +784,7 @@ def main():
             "frac": round(silu["gbs"] / pk["hbm_gbs"], 4), "peak_source": pk["source"],
             "traffic": ncu_traffic("silu_and_mul_T512"),
             "algorithmic_bytes": B_SILU}
-    e2e = e2e_chain(ch, ops, steps=min(args.steps, 50), warmup=3)
+    e2e = e2e_chain(ch, ops, steps=min(args.steps, 50), warmup=3, ws=ws)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
