@@ -428,6 +428,28 @@ def kv_reference_path(src_caches, dst_caches, src, dst, dev):
     return t1 - t0, t2 - t1
 
 
+def kv_host_path(sc, dc, sids, dids, steps, warmup):
+    """The KVhelper host round trip (DRAM swap-out of a preempted request and
+    swap-in, decode_llm_engine.py:31-40 / base_worker.py `_get_kv_cache_nofree`,
+    and the Ray-path get_kv_cache / insert_kv_cache): one gather kernel writing
+    every layer's blocks into page-locked host memory, one scatter kernel back."""
+    import torch
+
+    from paceserve_b200 import kv_transfer_ops as kvo
+
+    host = torch.empty(KV_L, sids.numel(), *KV_SLAB, dtype=torch.bfloat16, pin_memory=True)
+    nbytes = host.numel() * 2
+    ms_g = _time_copy(lambda: kvo.gather_blocks(list(sc), sids, host), steps, warmup)
+    for c in dc:
+        c.zero_()
+    ms_s = _time_copy(lambda: kvo.scatter_blocks(host, list(dc), dids), steps, warmup)
+    ok = all(torch.equal(dc[l][dids.long()], sc[l][sids.long()]) for l in range(KV_L))
+    return {"bytes": nbytes, "byte_exact": bool(ok),
+            "gather_to_host": {"ms": round(ms_g, 3), "gbs": round(nbytes / (ms_g * 1e-3) / 1e9, 1)},
+            "scatter_from_host": {"ms": round(ms_s, 3), "gbs": round(nbytes / (ms_s * 1e-3) / 1e9, 1)},
+            "round_trip_gbs": round(nbytes / ((ms_g + ms_s) * 1e-3) / 1e9, 2)}
+
+
 def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
     """LP->HP promotion on rank pairs (0->1, 2->3, ...): the HP rank pulls the
     request blocks from the LP rank's caches (CUDA IPC) with one kernel.  With one
@@ -455,6 +477,7 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
         ok = all(torch.equal(dc[l][dids.long()], sc[l][sids.long()]) for l in range(KV_L))
         out.update({"mode": "one GPU: HBM -> HBM", "blocks": int(len(src)), "bytes": nbytes,
                     "byte_exact": bool(ok), "methods": res})
+        out["host_path"] = kv_host_path(sc, dc, sids, dids, max(2, steps // 4), 2)
         if baseline:
             d2h, h2d = kv_reference_path(sc, dc, src, dst, dev)
             out["reference_path"] = {"gbs": round(nbytes / (d2h + h2d) / 1e9, 2),

@@ -64,12 +64,45 @@ __global__ void __launch_bounds__(512)
       prefetch_l2(key + tok * k_stride, (int64_t)num_kv_heads * head_size * sizeof(T));
   }
   pdl_wait();
-  const int64_t pos = positions[tok];
-  if (pos < 0 || pos >= max_position) return;
   const int embed = rot_dim / 2;
   // units per head: NeoX pairs a vector of each half; GPT-J one vector of pairs
   const int uph = NEOX ? embed / V : rot_dim / V;
   const int total = (num_heads + num_kv_heads) * uph;
+  if (NEOX && total <= (int)blockDim.x) {
+    // One unit per thread: issue the q/k loads before the position load so
+    // the two latencies overlap.
+    const int u = threadIdx.x;
+    const bool live = u < total;
+    const int head = live ? u / uph : 0;
+    const int part = live ? u - head * uph : 0;
+    T* hp = head < num_heads ? query + tok * q_stride + (int64_t)head * head_size
+                             : key + tok * k_stride + (int64_t)(head - num_heads) * head_size;
+    const int i0 = part * V;
+    uint4 xv = make_uint4(0, 0, 0, 0), yv = xv;
+    if (live) {
+      xv = ld_v4(hp + i0);
+      yv = ld_v4(hp + embed + i0);
+    }
+    const int64_t pos = positions[tok];
+    if (!live || pos < 0 || pos >= max_position) return;
+    const C* cos_row = cache + pos * rot_dim;
+    float c[V], s[V], x[V], y[V];
+    load_cs<C, V>(cos_row + i0, c);
+    load_cs<C, V>(cos_row + embed + i0, s);
+    Tr::unpack(xv, x);
+    Tr::unpack(yv, y);
+    float xo[V], yo[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      xo[e] = x[e] * c[e] - y[e] * s[e];
+      yo[e] = y[e] * c[e] + x[e] * s[e];
+    }
+    st_v4(hp + i0, Tr::pack(xo));
+    st_v4(hp + embed + i0, Tr::pack(yo));
+    return;
+  }
+  const int64_t pos = positions[tok];
+  if (pos < 0 || pos >= max_position) return;
   const C* cos_row = cache + pos * rot_dim;
   const C* sin_row = cos_row + embed;
   for (int u = threadIdx.x; u < total; u += blockDim.x) {
