@@ -362,6 +362,33 @@ def cpu_chain_sample(budget_s: float = 8.0, max_passes: int = 1 << 30, warmup: i
                       f"{n} layer>=1 passes ({t_sum:.1f} s), scaled to 32 layers"}
 
 
+def cpu_config1_sample(budget_s: float = 3.0):
+    """BASELINE config 1 on the host cores: one Llama-3-8B layer's ops in fp32 at
+    T=64 (fused_add_rms_norm -> neox rope -> silu_and_mul), the oracle's torch
+    formulas; wall time per chain and fp32 algorithmic bytes per second."""
+    import torch
+
+    from oracle import ops_ref
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    inp = ops_ref.config1_inputs(seed=0)
+    ops_ref.config1_chain(inp)
+    n, t_sum = 0, 0.0
+    while n < 3 or t_sum < budget_s:
+        t0 = time.perf_counter()
+        ops_ref.config1_chain(inp)
+        t_sum += time.perf_counter() - t0
+        n += 1
+    ms = t_sum / n * 1e3
+    nbytes = ops_ref.CONFIG1["T"] * ops_ref.CONFIG1_BYTES_PER_TOKEN
+    return {"workload": "config 1: one Llama-3-8B layer, fp32, T=64 (fused_add_rms_norm, neox "
+                        "rope q[64,32,128] k[64,8,128], silu_and_mul [64,28672])",
+            "ms_per_chain": round(ms, 3), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
+            "tokens_per_s": round(ops_ref.CONFIG1["T"] / (ms * 1e-3), 1), "cores": cores,
+            "passes": n}
+
+
 # ------------------------------------------------------------ KV promotion --
 KV_NB, KV_L, KV_SLAB = 8192, 32, (2, 16, 8, 128)
 KV_BLOCK_BYTES = 2 * 16 * 8 * 128 * 2
@@ -720,6 +747,7 @@ def run_reference(args, ws, rank):
         "config": {"workload": WORKLOAD, "tokens_per_step": T, "layers": L},
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_config1": cpu_config1_sample(),
     }
     print(json.dumps(line), flush=True)
 
@@ -827,6 +855,7 @@ def main():
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_chain_sample()
+        line["cpu_baseline"]["config1"] = cpu_config1_sample()
     if ws > 1:
         del ch
         torch.cuda.empty_cache()

@@ -234,3 +234,43 @@ def chain_layer(layer: int, bufs: dict, cache: torch.Tensor, positions: torch.Te
     out, res = fused_add_rms_norm_rounded(bufs["attn"], bufs["residual2"], bufs["w_post"], eps)
     bufs["attn"], bufs["residual2"] = out, res
     bufs["act"] = silu_and_mul_rounded(bufs["gate_up"])
+
+
+# ------------------------------------------- single-layer fp32 CPU chain --
+# The CPU-runnable configuration of the path: one Llama-3-8B decoder layer's
+# ops in fp32 at T=64 (residual add fused into the norm, llama.py:248-252;
+# rope as rotary_embedding.py:87-103 calls it; SwiGLU as activation.py:19-24).
+CONFIG1 = {"T": 64, "H": 4096, "NQ": 32, "NKV": 8, "HD": 128, "I": 14336, "EPS": 1e-5,
+           "THETA": 500000.0, "MAX_POS": 8192, "POS_HIGH": 4096}
+# fp32 algorithmic bytes per token: fused norm 16H, rope 8(nq+nkv)hd + rot*4 + 8,
+# silu_and_mul 12I.
+CONFIG1_BYTES_PER_TOKEN = 16 * 4096 + (8 * 40 * 128 + 128 * 4 + 8) + 12 * 14336
+
+
+def config1_inputs(seed: int = 0) -> dict:
+    """Seeded fp32 CPU inputs: x, residual [T,H] ~ N(0,1); w [H] ~ N(1,0.02);
+    q [T,NQ*HD], k [T,NKV*HD] ~ N(0,1); positions uniform in [0, 4096);
+    gate_up [T,2I] ~ N(0,1); the fp32 cos/sin cache for max_pos 8192."""
+    c = CONFIG1
+    g = torch.Generator().manual_seed(seed)
+    T, H = c["T"], c["H"]
+    return {
+        "x": torch.randn(T, H, generator=g),
+        "residual": torch.randn(T, H, generator=g),
+        "w": torch.randn(H, generator=g) * 0.02 + 1.0,
+        "q": torch.randn(T, c["NQ"] * c["HD"], generator=g),
+        "k": torch.randn(T, c["NKV"] * c["HD"], generator=g),
+        "positions": torch.randint(0, c["POS_HIGH"], (T,), generator=g),
+        "gate_up": torch.randn(T, 2 * c["I"], generator=g),
+        "cache": cos_sin_cache(c["HD"], c["MAX_POS"], c["THETA"]),
+    }
+
+
+def config1_chain(inp: dict) -> dict:
+    """fused_add_rms_norm -> neox rotary_embedding -> silu_and_mul in fp32.
+    Returns the outputs: normed x, updated residual, rotated q and k, act."""
+    c = CONFIG1
+    x, res = fused_add_rms_norm_fp32(inp["x"], inp["residual"], inp["w"], c["EPS"])
+    q, k = rotary_embedding_fp32(inp["positions"], inp["q"], inp["k"], c["HD"], inp["cache"], True)
+    act = silu_and_mul_fp32(inp["gate_up"])
+    return {"x": x, "residual": res, "q": q, "k": k, "act": act}

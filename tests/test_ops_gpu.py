@@ -256,3 +256,21 @@ def test_graph_capture_of_op_chain():
     out_ref, res_ref = ops_ref.fused_add_rms_norm_rounded(x0.cpu(), r0.cpu(), w.cpu(), 1e-5)
     assert torch.equal(r.cpu(), res_ref)
     assert_matches_rounded(x, out_ref, torch.bfloat16)
+
+
+def test_config1_layer_chain_fp32():
+    """The CPU-runnable configuration (one Llama-3-8B layer in fp32 at T=64:
+    fused_add_rms_norm -> neox rope -> silu_and_mul) on the GPU against the
+    oracle's fp32 chain on the same seeded inputs; fp32 outputs within 1e-5."""
+    c = ops_ref.CONFIG1
+    inp = ops_ref.config1_inputs(seed=0)
+    ref = ops_ref.config1_chain(inp)
+    d = {k: v.to(DEV) for k, v in inp.items()}
+    layernorm_ops.fused_add_rms_norm(d["x"], d["residual"], d["w"], c["EPS"])
+    pos_encoding_ops.rotary_embedding(d["positions"], d["q"], d["k"], c["HD"], d["cache"], True)
+    act = torch.empty(c["T"], c["I"], device=DEV)
+    activation_ops.silu_and_mul(act, d["gate_up"])
+    torch.cuda.synchronize()
+    got = {"x": d["x"], "residual": d["residual"], "q": d["q"], "k": d["k"], "act": act}
+    for name, r in ref.items():
+        assert rel_err(got[name], r) <= 1e-5, name

@@ -159,3 +159,27 @@ def test_oracle_against_reference_golden(path):
         # 16-bit: >= 98% bit-equal, the rest within 2 ulps at the largest output;
         # fp32: within 1e-5 (CPU and GPU exp/tanh differ in the last ulps)
         assert_matches_rounded(got, ref, dtype)
+
+
+def test_config1_chain_properties():
+    """The fp32 single-layer chain: residual = x + r exactly; the normalised row
+    divided by the weight has unit RMS; rope preserves every rotated pair's
+    norm; silu_and_mul matches a float64 evaluation."""
+    c = ops_ref.CONFIG1
+    inp = ops_ref.config1_inputs(seed=0)
+    out = ops_ref.config1_chain(inp)
+    assert torch.equal(out["residual"], inp["x"] + inp["residual"])
+    rms = (out["x"] / inp["w"]).pow(2).mean(-1).sqrt()
+    assert torch.allclose(rms, torch.ones_like(rms), atol=1e-4)
+    hd, half = c["HD"], c["HD"] // 2
+    for name, heads in (("q", c["NQ"]), ("k", c["NKV"])):
+        a = inp[name].reshape(c["T"], heads, hd)
+        b = out[name].reshape(c["T"], heads, hd)
+        na = a[..., :half] ** 2 + a[..., half:] ** 2
+        nb = b[..., :half] ** 2 + b[..., half:] ** 2
+        assert torch.allclose(na, nb, rtol=1e-4, atol=1e-5)
+    g = inp["gate_up"].double()
+    a64, b64 = g[:, : c["I"]], g[:, c["I"]:]
+    act64 = a64 / (1 + torch.exp(-a64)) * b64
+    assert (out["act"].double() - act64).abs().max().item() <= 1e-5 * act64.abs().max().item()
+    assert ops_ref.CONFIG1_BYTES_PER_TOKEN == 279048
