@@ -83,3 +83,33 @@ def test_check_raises_pace_error():
     rc = lib.pace_silu_and_mul(None, None, -3, 8, 16, 8, cabi.PACE_F16, None)
     with pytest.raises(cabi.PaceError, match="bad shape"):
         cabi.check(rc)
+
+
+def test_last_error_is_per_thread():
+    """pace_last_error() is thread-local: concurrent callers (the reference's
+    KV insertion threads, decode_instance.py:50-51) each read their own message."""
+    import threading
+
+    lib = cabi.load()
+    barrier = threading.Barrier(2)
+    seen = {}
+
+    def norm_caller():
+        rc = lib.pace_rms_norm(None, None, None, 1e-5, -1, 8, 8, 8, cabi.PACE_BF16, None)
+        barrier.wait()  # the other thread has now failed too
+        barrier.wait()
+        seen["norm"] = (rc, lib.pace_last_error().decode())
+
+    def topk_caller():
+        barrier.wait()
+        rc = lib.pace_topk_softmax(None, None, None, None, 4, 8, 9, 0, None)
+        barrier.wait()
+        seen["topk"] = (rc, lib.pace_last_error().decode())
+
+    ts = [threading.Thread(target=norm_caller), threading.Thread(target=topk_caller)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert seen["norm"][0] == cabi.PACE_ERR_INVALID_ARGUMENT and "rms_norm" in seen["norm"][1]
+    assert seen["topk"][0] == cabi.PACE_ERR_INVALID_ARGUMENT and "num_experts" in seen["topk"][1]

@@ -131,3 +131,45 @@ def test_copy_blocks_across_gpus(push, method):
     torch.cuda.synchronize("cuda:0")
     torch.cuda.synchronize("cuda:1")
     check_copied(src, dst, before, sids, dids)
+
+
+def test_concurrent_gather_scatter_from_threads():
+    """Four host threads, each on its own stream, gather different requests to
+    pinned memory and scatter them into another cache at the same time (the
+    reference runs 4 KV insertion threads, decode_instance.py:50-51, and
+    `_get_kv_cache` concurrently from Ray threads).  Every copy is byte-exact
+    and untouched blocks stay untouched."""
+    import threading
+
+    L, nb, n = 4, 512, 40
+    src = make_cache(L, nb, seed=21)
+    dst = make_cache(L, nb, seed=22)
+    before = [d.clone() for d in dst]
+    perm_s = torch.randperm(nb, generator=torch.Generator().manual_seed(23))
+    perm_d = torch.randperm(nb, generator=torch.Generator().manual_seed(24))
+    jobs = [(perm_s[i * n:(i + 1) * n].to(torch.int32), perm_d[i * n:(i + 1) * n].to(torch.int32))
+            for i in range(4)]
+    errors = []
+
+    def worker(sids, dids):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                host = torch.empty(L, n, 2, 16, 8, 128, dtype=torch.bfloat16, pin_memory=True)
+                for _ in range(3):
+                    kv.gather_blocks(src, sids.cuda(non_blocking=False), host)
+                    kv.scatter_blocks(host, dst, dids.cuda(non_blocking=False))
+                s.synchronize()
+        except Exception as exc:  # reported to the main thread
+            errors.append(exc)
+
+    ts = [threading.Thread(target=worker, args=j) for j in jobs]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    all_s = torch.cat([j[0] for j in jobs])
+    all_d = torch.cat([j[1] for j in jobs])
+    check_copied(src, dst, before, all_s, all_d)
