@@ -24,7 +24,9 @@ namespace pace {
 namespace {
 
 constexpr int kAppendThreads = 256;
-constexpr int kMaxSmemIndptr = 8192;  // append_indptr entries staged in shared memory
+// Requests whose per-request metadata (append_indptr, kv_indptr,
+// kv_last_page_len) each CTA stages in shared memory: 3 x 2049 x 4 B.
+constexpr int64_t kMaxStagedBatch = 2048;
 
 struct AppendJob {
   int64_t nnz;
@@ -38,16 +40,17 @@ struct AppendJob {
   int64_t num_indices;  // entries of kv_indices
 };
 
-// Page and slot of token i, or false if any index is out of range.
+// Page and slot of a token of request b at sequence position pos, or false
+// if any index is out of range.  ip / last: kv_indptr and kv_last_page_len
+// (global or staged copies).
 __device__ __forceinline__ bool locate_token(const AppendJob& j, int b, int64_t pos,
-                                             const int32_t* kv_indices, const int32_t* kv_indptr,
-                                             const int32_t* kv_last_page_len, int64_t* page,
-                                             int* slot) {
+                                             const int32_t* kv_indices, const int32_t* ip,
+                                             const int32_t* last, int64_t* page, int* slot) {
   if (b < 0 || b >= j.batch || pos < 0) return false;
-  const int64_t p0 = kv_indptr[b];
-  const int64_t np = (int64_t)kv_indptr[b + 1] - p0;
+  const int64_t p0 = ip[b];
+  const int64_t np = (int64_t)ip[b + 1] - p0;
   if (np <= 0 || p0 < 0 || p0 + np > j.num_indices) return false;
-  const int64_t seq_len = (np - 1) * j.page_size + kv_last_page_len[b];
+  const int64_t seq_len = (np - 1) * j.page_size + last[b];
   if (pos >= seq_len) return false;
   const int64_t pg = kv_indices[p0 + pos / j.page_size];
   if (pg < 0 || pg >= j.num_pages) return false;
@@ -71,14 +74,17 @@ __device__ __forceinline__ int find_request(const int32_t* indptr, int64_t batch
 
 // BY_INDPTR: derive (request, position) from append_indptr; otherwise read
 // batch_indices / positions.  VEC: 16-byte vectors; otherwise elements.
-template <typename T, bool BY_INDPTR, bool VEC>
+// STAGED: the per-request arrays are copied to shared memory first, so the
+// token's index chain after the K/V loads is shared-memory lookups plus one
+// global load (its kv_indices entry) instead of three dependent global loads.
+template <typename T, bool BY_INDPTR, bool VEC, bool STAGED>
 __global__ void __launch_bounds__(kAppendThreads)
     kv_append_kernel(const T* key, const T* value, const int32_t* __restrict__ batch_indices,
                      const int32_t* __restrict__ positions, const int32_t* __restrict__ append_indptr,
                      T* cache, const int32_t* __restrict__ kv_indices,
                      const int32_t* __restrict__ kv_indptr,
                      const int32_t* __restrict__ kv_last_page_len, AppendJob job, int32_t* bad) {
-  extern __shared__ int32_t sh_indptr[];
+  extern __shared__ int32_t sh[];  // STAGED: kv_indptr | kv_last_page_len | append_indptr
   constexpr int V = VEC ? Traits<T>::kVec : 1;
   const int64_t i = blockIdx.x;
   const int64_t row = (int64_t)job.heads * job.head_dim;  // elements per K (or V) row
@@ -89,11 +95,26 @@ __global__ void __launch_bounds__(kAppendThreads)
     prefetch_l2(value + i * job.value_stride, row * (int64_t)sizeof(T));
   }
   pdl_wait();
-  const bool smem_indptr = BY_INDPTR && job.batch + 1 <= kMaxSmemIndptr;
-  if (smem_indptr) {
-    for (int64_t k = threadIdx.x; k <= job.batch; k += blockDim.x) sh_indptr[k] = append_indptr[k];
+  // Token -> request and position inputs that need no staged data.
+  int b = 0;
+  int64_t pos = 0;
+  if (!BY_INDPTR) {
+    b = batch_indices[i];
+    pos = positions[i];
+  }
+  int32_t* s_ip = sh;
+  int32_t* s_last = sh + job.batch + 1;
+  int32_t* s_ai = sh + 2 * job.batch + 1;
+  if (STAGED) {
+    for (int64_t k = threadIdx.x; k <= job.batch; k += blockDim.x) {
+      s_ip[k] = kv_indptr[k];
+      if (k < job.batch) s_last[k] = kv_last_page_len[k];
+      if (BY_INDPTR) s_ai[k] = append_indptr[k];
+    }
     __syncthreads();
   }
+  const int32_t* ip = STAGED ? s_ip : kv_indptr;
+  const int32_t* last = STAGED ? s_last : kv_last_page_len;
   for (int64_t u0 = 0; u0 < 2 * units; u0 += blockDim.x) {
     const int64_t u = u0 + threadIdx.x;
     const bool is_v = u >= units;
@@ -108,21 +129,16 @@ __global__ void __launch_bounds__(kAppendThreads)
       else
         elem = *src;
     }
-    int b;
-    int64_t pos;
     if (BY_INDPTR) {
-      const int32_t* ip = smem_indptr ? sh_indptr : append_indptr;
-      b = find_request(ip, job.batch, i);
-      const int64_t np = (int64_t)kv_indptr[b + 1] - kv_indptr[b];
-      const int64_t seq_len = (np - 1) * job.page_size + kv_last_page_len[b];
-      pos = seq_len - ((int64_t)ip[b + 1] - ip[b]) + (i - ip[b]);
-    } else {
-      b = batch_indices[i];
-      pos = positions[i];
+      const int32_t* ai = STAGED ? s_ai : append_indptr;
+      b = find_request(ai, job.batch, i);
+      const int64_t np = (int64_t)ip[b + 1] - ip[b];
+      const int64_t seq_len = (np - 1) * job.page_size + last[b];
+      pos = seq_len - ((int64_t)ai[b + 1] - ai[b]) + (i - ai[b]);
     }
     int64_t page;
     int slot;
-    const bool ok = locate_token(job, b, pos, kv_indices, kv_indptr, kv_last_page_len, &page, &slot);
+    const bool ok = locate_token(job, b, pos, kv_indices, ip, last, &page, &slot);
     if (!ok) {
       if (bad && u0 == 0 && threadIdx.x == 0) atomicAdd(bad, 1);
       return;
@@ -159,7 +175,8 @@ int run_append(const void* key, const void* value, int64_t nnz, int heads, int h
   StreamDeviceGuard guard(stream);
   AppendJob job{nnz, heads, head_dim, key_stride, value_stride, num_pages, page_size, batch,
                 num_indices};
-  const size_t smem = BY_INDPTR && batch + 1 <= kMaxSmemIndptr ? (size_t)(batch + 1) * 4 : 0;
+  const bool staged = batch <= kMaxStagedBatch;
+  const size_t smem = staged ? (size_t)(3 * batch + 2) * 4 : 0;
   return PACE_DISPATCH_FLOAT(dtype, what, [&] {
     using T = scalar_t;
     constexpr int V = Traits<T>::kVec;
@@ -170,15 +187,18 @@ int run_append(const void* key, const void* value, int64_t nnz, int heads, int h
     const T* k = static_cast<const T*>(key);
     const T* v = static_cast<const T*>(value);
     T* c = static_cast<T*>(cache);
+    auto go = [&](auto kernel) {
+      return launch(kernel, dim3((unsigned)nnz), dim3(threads), smem, stream, k, v, batch_indices,
+                    positions, append_indptr, c, kv_indices, kv_indptr, kv_last_page_len, job,
+                    bad);
+    };
     cudaError_t err;
     if (vec)
-      err = launch(kv_append_kernel<T, BY_INDPTR, true>, dim3((unsigned)nnz), dim3(threads), smem,
-                   stream, k, v, batch_indices, positions, append_indptr, c, kv_indices, kv_indptr,
-                   kv_last_page_len, job, bad);
+      err = staged ? go(kv_append_kernel<T, BY_INDPTR, true, true>)
+                   : go(kv_append_kernel<T, BY_INDPTR, true, false>);
     else
-      err = launch(kv_append_kernel<T, BY_INDPTR, false>, dim3((unsigned)nnz), dim3(threads),
-                   smem, stream, k, v, batch_indices, positions, append_indptr, c, kv_indices,
-                   kv_indptr, kv_last_page_len, job, bad);
+      err = staged ? go(kv_append_kernel<T, BY_INDPTR, false, true>)
+                   : go(kv_append_kernel<T, BY_INDPTR, false, false>);
     if (err != cudaSuccess) return cuda_fail(err, what);
     return PACE_OK;
   });

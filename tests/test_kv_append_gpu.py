@@ -154,3 +154,30 @@ def test_append_matches_flashinfer_when_available():
     kv.append_paged_kv_cache(k, v, bi, po, c, ki, kp, kl)
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(c, b)
+
+
+@pytest.mark.parametrize("form", ["indices", "indptr"])
+def test_append_large_batch_unstaged(form):
+    """More than 2048 requests: the per-request metadata is read from global
+    memory instead of being staged in shared memory; same bytes."""
+    rng = np.random.default_rng(12)
+    nkv, hd, P, ps = 2, 64, 7000, 16
+    ai, kp, ki, kl = mixed_batch(rng, ps, P, prefills=((30, 5),), decodes=2100, max_ctx=40)
+    assert kp.numel() - 1 > 2048
+    nnz = int(ai[-1])
+    key = torch.randn(nnz, nkv * hd).bfloat16()
+    value = torch.randn(nnz, nkv * hd).bfloat16()
+    cache = torch.zeros(P, 2, ps, nkv, hd).bfloat16()
+    bi, pos = append_ref.get_batch_indices_positions(ai, append_ref.get_seq_lens(kp, kl, ps), nnz)
+    ref = append_ref.append_paged_kv_cache(key, value, bi, pos, cache.clone(), ki, kp, kl)
+    got = cache.to(DEV)
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    if form == "indices":
+        kv.append_paged_kv_cache(key.to(DEV), value.to(DEV), bi.to(DEV), pos.to(DEV), got,
+                                 ki.to(DEV), kp.to(DEV), kl.to(DEV), "NHD", bad)
+    else:
+        kv.append_paged_kv_cache_by_indptr(key.to(DEV), value.to(DEV), ai.to(DEV), got, ki.to(DEV),
+                                           kp.to(DEV), kl.to(DEV), bad)
+    torch.cuda.synchronize()
+    assert bad.item() == 0
+    assert torch.equal(got.cpu(), ref)
