@@ -487,8 +487,8 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
     from paceserve_b200 import kv_transfer as kvt
 
     dev = torch.device(f"cuda:{local}")
-    out = {"workload": "LP->HP KV promotion, Llama-3-8B paged cache [8192, 2, 16, 8, 128] bf16 x 32 "
-                       "layers, 8 requests lognormal(6.9, 0.7) capped 8192, 80 % occupied"}
+    out = {"workload": f"LP->HP KV promotion, Llama-3-8B paged cache [{KV_NB}, 2, 16, 8, 128] bf16 x "
+                       "32 layers, 8 requests lognormal(6.9, 0.7) capped 8192, 80 % occupied"}
     if ws == 1:
         lens, src, dst = kv_requests(7)
         sc = _kv_caches(dev, fill_seed=100)
@@ -779,17 +779,21 @@ def run_side_workload(args, ws, rank, local):
 
 
 def main():
+    global KV_NB
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-blocks", type=int, default=8192,
+                    help="blocks per layer of the kv workload's caches (a smaller case for ncu)")
     ap.add_argument("--workload", choices=["chain", "kv", "sweep", "moe"], default="chain",
                     help="chain: the driver's line (config 2); kv: LP->HP promotion (config 5); "
                          "sweep: per-op token sweep (config 3); moe: routing (config 4)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    KV_NB = args.kv_blocks
     ws, rank, local = init_dist()
     if args.impl == "ours" and args.workload != "chain":
         run_side_workload(args, ws, rank, local)
