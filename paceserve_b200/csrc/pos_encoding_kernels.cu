@@ -58,20 +58,31 @@ __global__ void __launch_bounds__(512)
   constexpr int V = Tr::kVec;
   const int64_t tok = blockIdx.x;
   pdl_launch_dependents();
-  if (threadIdx.x == 0) {
-    prefetch_l2(query + tok * q_stride, (int64_t)num_heads * head_size * sizeof(T));
-    if (num_kv_heads > 0)
-      prefetch_l2(key + tok * k_stride, (int64_t)num_kv_heads * head_size * sizeof(T));
-  }
-  pdl_wait();
   const int embed = rot_dim / 2;
   // units per head: NeoX pairs a vector of each half; GPT-J one vector of pairs
   const int uph = NEOX ? embed / V : rot_dim / V;
   const int total = (num_heads + num_kv_heads) * uph;
-  if (NEOX && total <= (int)blockDim.x) {
-    // One unit per thread: issue the q/k loads before the position load so
-    // the two latencies overlap.
-    const int u = threadIdx.x;
+  if (threadIdx.x == 0) {
+    // Prefetch the heads this CTA rotates (all of them when gridDim.y == 1).
+    const int u0 = blockIdx.y * blockDim.x;
+    const int u1 = gridDim.y == 1 ? total : min(total, u0 + (int)blockDim.x);
+    if (u1 > u0) {
+      const int ha = u0 / uph, hb = (u1 - 1) / uph;  // heads [ha, hb]
+      const int qb = min(hb, num_heads - 1);
+      if (qb >= ha)
+        prefetch_l2(query + tok * q_stride + (int64_t)ha * head_size,
+                    (int64_t)(qb - ha + 1) * head_size * sizeof(T));
+      const int ka = max(ha, num_heads) - num_heads, kb = hb - num_heads;
+      if (kb >= ka)
+        prefetch_l2(key + tok * k_stride + (int64_t)ka * head_size,
+                    (int64_t)(kb - ka + 1) * head_size * sizeof(T));
+    }
+  }
+  pdl_wait();
+  if (NEOX && total <= (int)(blockDim.x * gridDim.y)) {
+    // One unit per thread (the token's units split over gridDim.y CTAs): issue
+    // the q/k loads before the position load so the two latencies overlap.
+    const int u = blockIdx.y * blockDim.x + threadIdx.x;
     const bool live = u < total;
     const int head = live ? u / uph : 0;
     const int part = live ? u - head * uph : 0;
@@ -195,13 +206,23 @@ int launch_rope(const int64_t* positions, void* query, void* key, int64_t num_to
     vec = vec && (embed % V == 0);
   else
     vec = vec && (rot_dim % V == 0);
-  const dim3 grid((unsigned)num_tokens);
+  dim3 grid((unsigned)num_tokens);
   cudaError_t err;
   if (vec) {
     const int uph = neox ? embed / V : rot_dim / V;
-    int threads = (int)ceil_div((int64_t)(num_heads + num_kv_heads) * uph, 32) * 32;
+    const int64_t units = (int64_t)(num_heads + num_kv_heads) * uph;
+    // NeoX: a token's units (one per thread) may be split over gridDim.y CTAs.
+    // Measured on B200 (Llama-3-8B, 320 units): 2-warp CTAs are fastest for
+    // decode-sized batches (T <= 128: 13-18 % over one CTA per token), one CTA
+    // per token at T ~ 512, 5-warp CTAs for long prefills (T > 1024: 9 %).
+    int64_t per_cta = 512;
+    if (neox) per_cta = num_tokens <= 128 ? 64 : (num_tokens > 1024 ? 160 : 512);
+    int64_t split = neox ? ceil_div(units, per_cta) : 1;
+    if (split > 65535) split = 1;  // grid.y limit: one CTA per token loops over the units
+    int threads = (int)ceil_div(ceil_div(units, split), 32) * 32;
     if (threads > 512) threads = 512;
     if (threads < 32) threads = 32;
+    grid.y = (unsigned)split;
     err = neox ? launch(rope_vec_kernel<T, C, true>, grid, dim3(threads), 0, stream, positions, q,
                         k, num_heads, num_kv_heads, head_size, q_stride, k_stride, cs, rot_dim,
                         max_position)
