@@ -122,6 +122,88 @@ __global__ void __launch_bounds__(kMaxThreads)
   }
 }
 
+// Plain rms_norm, R rows per CTA: each thread holds NV vectors of each of the
+// R rows, so a CTA has R times the bytes in flight of the one-row kernel and
+// one barrier serves R rows.  Rows past `rows` (the last CTA) are skipped.
+template <typename T, int NV, int R>
+__global__ void __launch_bounds__(kMaxThreads)
+    rms_norm_rows_kernel(const T* __restrict__ x_in, T* __restrict__ x_out,
+                         const T* __restrict__ weight, float eps, int hidden, int64_t rows,
+                         int64_t in_stride, int64_t out_stride) {
+  using Tr = Traits<T>;
+  constexpr int V = Tr::kVec;
+  __shared__ float red[R][32];
+  const int64_t row0 = (int64_t)blockIdx.x * R;
+  const int nvec = hidden / V;
+  pdl_launch_dependents();
+  if (threadIdx.x < R && row0 + threadIdx.x < rows)
+    prefetch_l2(x_in + (row0 + threadIdx.x) * in_stride, (int64_t)hidden * sizeof(T));
+  if (threadIdx.x == R && blockIdx.x < 4) prefetch_l2(weight, (int64_t)hidden * sizeof(T));
+  pdl_wait();
+
+  uint4 raw[R][NV];
+  uint4 wraw[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = threadIdx.x + j * blockDim.x;
+    if (c < nvec) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (row0 + r < rows) raw[r][j] = ld_nc_v4(x_in + (row0 + r) * in_stride + (int64_t)c * V);
+      wraw[j] = __ldg(reinterpret_cast<const uint4*>(weight) + c);
+    }
+  }
+  float ss[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    ss[r] = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = threadIdx.x + j * blockDim.x;
+      if (c < nvec && row0 + r < rows) {
+        float v[V];
+        Tr::unpack(raw[r][j], v);
+#pragma unroll
+        for (int e = 0; e < V; ++e) ss[r] += v[e] * v[e];
+      }
+    }
+    ss[r] = warp_sum(ss[r]);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) red[r][warp] = ss[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (row0 + r >= rows) break;
+    float total = 0.f;
+    for (int i = 0; i < nwarps; ++i) total += red[r][i];
+    const float inv = rsqrtf(total / (float)hidden + eps);
+    T* orow = x_out + (row0 + r) * out_stride;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = threadIdx.x + j * blockDim.x;
+      if (c < nvec) {
+        float v[V], w[V], o[V];
+        Tr::unpack(raw[r][j], v);
+        Tr::unpack(wraw[j], w);
+#pragma unroll
+        for (int e = 0; e < V; ++e) o[e] = Tr::round(v[e] * inv) * w[e];
+        st_v4(orow + (int64_t)c * V, Tr::pack(o));
+      }
+    }
+  }
+}
+
+// Rows per CTA of the plain norm's vector path (1 = rms_norm_vec_kernel).
+// Measured on B200: two rows per CTA are 8-9 % faster (8B) and 3-4 % faster
+// (70B) at T >= 8192, 5 % slower at T = 2048 and 45 % slower at T = 512, where
+// halving the CTA count leaves SMs idle.
+inline int norm_rows_per_cta(int64_t num_tokens) { return num_tokens >= 8192 ? 2 : 1; }
+
 // Scalar fallback for any hidden size, stride or alignment.
 template <typename T, bool FUSED>
 __global__ void __launch_bounds__(256)
@@ -177,6 +259,24 @@ int launch_norm(const void* x_in, void* x_out, void* res, const void* weight, fl
     int threads = (int)ceil_div(ceil_div(nvec, nv), 32) * 32;
     if (threads > kMaxThreads) threads = kMaxThreads;
     const int h = (int)hidden;
+    const int rows_per_cta = FUSED ? 1 : norm_rows_per_cta(num_tokens);
+    if (!FUSED && rows_per_cta > 1) {
+      const dim3 g((unsigned)ceil_div(num_tokens, (int64_t)rows_per_cta));
+      switch (nv * 10 + rows_per_cta) {
+#define PACE_ROWS_CASE(N, R)                                                                  \
+  case N * 10 + R:                                                                            \
+    err = launch(rms_norm_rows_kernel<T, N, R>, g, dim3(threads), 0, stream, xi, xo, w, eps, h, \
+                 num_tokens, in_stride, out_stride);                                          \
+    break;
+        PACE_ROWS_CASE(1, 2)
+        PACE_ROWS_CASE(2, 2)
+        PACE_ROWS_CASE(4, 2)
+#undef PACE_ROWS_CASE
+        default: return fail(PACE_ERR_INVALID_ARGUMENT, "%s: internal row split", name);
+      }
+      if (err != cudaSuccess) return cuda_fail(err, name);
+      return PACE_OK;
+    }
     switch (nv) {
 #define PACE_NORM_CASE(N)                                                                     \
   case N:                                                                                     \

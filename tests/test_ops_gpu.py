@@ -43,6 +43,19 @@ def test_rms_norm(T, H, dtype):
         assert_matches_rounded(out, ro, dtype, min_equal=0.99)
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("T,H", [(8193, 4096), (8192, 8192), (8195, 1024)])
+def test_rms_norm_two_rows_per_cta(T, H, dtype):
+    """T >= 8192 runs two rows per CTA; odd T leaves the last CTA one row."""
+    x = randn(T, H, dtype=dtype, seed=T + H)
+    w = randn(H, dtype=dtype, seed=2, mean=1.0, std=0.02)
+    out = torch.full((T + 1, H), 7.0, dtype=dtype, device=DEV)  # one guard row
+    layernorm_ops.rms_norm(out[:T], x.to(DEV), w.to(DEV), 1e-5)
+    assert rel_err(out[:T], ops_ref.rms_norm_fp32(x, w, 1e-5)) <= REL_TOL
+    assert_matches_rounded(out[:T], ops_ref.rms_norm_rounded(x, w, 1e-5), dtype)
+    assert bool((out[T] == 7.0).all())
+
+
 def test_rms_norm_empty_and_strided():
     x = randn(0, 4096).to(DEV)
     layernorm_ops.rms_norm(torch.empty_like(x), x, torch.ones(4096, dtype=x.dtype, device=DEV), 1e-5)
