@@ -44,9 +44,12 @@ def test_rms_norm(T, H, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("T,H", [(8193, 4096), (8192, 8192), (8195, 1024)])
-def test_rms_norm_two_rows_per_cta(T, H, dtype):
-    """T >= 8192 runs two rows per CTA; odd T leaves the last CTA one row."""
+@pytest.mark.parametrize("T,H", [(8193, 4096), (8192, 8192), (8195, 1024), (1024, 4096),
+                                 (3001, 4096), (2048, 1024)])
+def test_rms_norm_large_batch_shapes(T, H, dtype):
+    """Large-batch launch shapes of the plain norm: T >= 8192 runs two rows per
+    CTA (odd T leaves the last CTA one row); 1024 <= T < 8192 runs 128-thread
+    CTAs with up to 4 vectors per thread."""
     x = randn(T, H, dtype=dtype, seed=T + H)
     w = randn(H, dtype=dtype, seed=2, mean=1.0, std=0.02)
     out = torch.full((T + 1, H), 7.0, dtype=dtype, device=DEV)  # one guard row
