@@ -161,7 +161,8 @@ GATED = {
 
 @pytest.mark.parametrize("name", list(GATED))
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("T,d", [(1, 14336), (7, 14336), (512, 14336), (64, 28672), (3, 100), (5, 8)])
+@pytest.mark.parametrize("T,d", [(1, 14336), (7, 14336), (512, 14336), (64, 28672), (3, 100), (5, 8),
+                                 (65537, 64)])  # > 65535 rows: row-major grid
 def test_gated_activations(name, dtype, T, d):
     op, f32, rounded = GATED[name]
     x = randn(T, 2 * d, dtype=dtype, seed=T + d)
