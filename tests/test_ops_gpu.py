@@ -105,7 +105,11 @@ def _rope_case(T, nq, nkv, hd, rot, dtype, cache_dtype, neox, seed, max_pos=8192
                                                (torch.float32, torch.float32)])
 @pytest.mark.parametrize("T,nq,nkv,hd,rot", [(1, 32, 8, 128, 128), (512, 32, 8, 128, 128),
                                              (17, 64, 8, 128, 128), (9, 8, 2, 128, 64),
-                                             (5, 4, 4, 80, 80), (3, 4, 2, 72, 24)])
+                                             (5, 4, 4, 80, 80), (3, 4, 2, 72, 24),
+                                             # NeoX launch shapes: token-major parts (70B
+                                             # at mid T, any model at long prefill)
+                                             (300, 64, 8, 128, 128), (2049, 32, 8, 128, 128),
+                                             (1500, 64, 8, 128, 128)])
 def test_rotary_embedding(T, nq, nkv, hd, rot, dtype, cache_dtype, neox):
     qkv, q, k, cache, pos = _rope_case(T, nq, nkv, hd, rot, dtype, cache_dtype, neox, seed=T + nq)
     q0, k0, v0 = q.cpu().clone(), k.cpu().clone(), qkv[:, (nq + nkv) * hd:].cpu().clone()
