@@ -181,3 +181,47 @@ def test_append_large_batch_unstaged(form):
     torch.cuda.synchronize()
     assert bad.item() == 0
     assert torch.equal(got.cpu(), ref)
+
+
+@pytest.mark.parametrize("extra_block", [False, True])
+def test_promoted_request_keeps_decoding(extra_block):
+    """A running request moves LP -> HP mid-decode and continues there.
+
+    The LP worker holds 37 tokens of a request (blocks of 16, 16 and 5 tokens) in random
+    blocks of every layer. The HP worker allocates its table the way
+    BaseWorker._insert_kv_cache does (base_worker.py:255-277); with `extra_block`
+    that table is one block longer than the sender's. align_block_tables maps the
+    transfer, the promotion kernel copies the blocks, and the paged-KV append writes
+    decode token 38 into the HP cache. The HP cache must then hold the 38-token
+    sequence exactly, as if the request had run on HP from the start.
+    """
+    from paceserve_b200 import kv_transfer as kvt
+
+    L, P, ps, nkv, hd = 3, 64, 16, 8, 128
+    g = torch.Generator().manual_seed(31)
+    lp = [torch.randn(P, 2, ps, nkv, hd, generator=g).bfloat16().to(DEV) for _ in range(L)]
+    hp = [torch.zeros(P, 2, ps, nkv, hd, dtype=torch.bfloat16, device=DEV) for _ in range(L)]
+    lp_table = [41, 7, 19]                       # 37 tokens: 16 + 16 + 5
+    hp_table = [3, 58, 22] + ([9] if extra_block else [])
+    dst = kvt.align_block_tables(len(lp_table), hp_table)
+    kvt.promote(lp, hp, lp_table, dst)
+    # decode token 38 on HP: page table = the aligned blocks, last page holds 6
+    k_new = torch.randn(1, nkv * hd, generator=g).bfloat16().to(DEV)
+    v_new = torch.randn(1, nkv * hd, generator=g).bfloat16().to(DEV)
+    ai = torch.tensor([0, 1], dtype=torch.int32, device=DEV)
+    kp = torch.tensor([0, 3], dtype=torch.int32, device=DEV)
+    kl = torch.tensor([6], dtype=torch.int32, device=DEV)
+    ki = torch.tensor(dst, dtype=torch.int32, device=DEV)
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for l in range(L):
+        kv.append_paged_kv_cache_by_indptr(k_new, v_new, ai, hp[l], ki, kp, kl, bad)
+    torch.cuda.synchronize()
+    assert bad.item() == 0
+    for l in range(L):
+        for j, (s, d) in enumerate(zip(lp_table, dst)):
+            n = 16 if j < 2 else 5
+            assert torch.equal(hp[l][d, :, :n].cpu(), lp[l][s, :, :n].cpu())
+        assert torch.equal(hp[l][dst[2], 0, 5].cpu(), k_new.view(nkv, hd).cpu())
+        assert torch.equal(hp[l][dst[2], 1, 5].cpu(), v_new.view(nkv, hd).cpu())
+        untouched = [b for b in range(P) if b not in dst]
+        assert int(hp[l][untouched].ne(0).sum()) == 0
