@@ -52,8 +52,12 @@ __device__ __forceinline__ void load_cs(const C* p, float* out) {
 // SPLIT_MAJOR: the token's units are split over several CTAs ("parts") and
 // the grid is (parts, tokens); otherwise it is (tokens, parts).  A compile-time
 // choice: selecting the indices at run time cost 12 registers and occupancy.
-template <typename T, typename C, bool NEOX, bool SPLIT_MAJOR>
-__global__ void __launch_bounds__(512)
+// TIGHT: at most 32 registers (4 CTAs of 512 threads per SM), for the
+// multi-part launches above T = 128, where the extra residency pays: 70B at
+// T=512 16 % faster, long prefills 1-4 %.  One-part launches keep the
+// compiler's 40 registers (32 cost the 8B shape at T=512 26 %).
+template <typename T, typename C, bool NEOX, bool SPLIT_MAJOR, bool TIGHT>
+__global__ void __launch_bounds__(512, TIGHT ? 4 : 0)
     rope_vec_kernel(const int64_t* __restrict__ positions, T* query, T* key, int num_heads,
                     int num_kv_heads, int head_size, int64_t q_stride, int64_t k_stride,
                     const C* __restrict__ cache, int rot_dim, int64_t max_position) {
@@ -239,8 +243,11 @@ int launch_rope(const int64_t* positions, void* query, void* key, int64_t num_to
       return launch(kernel, grid, dim3(threads), 0, stream, positions, q, k, num_heads,
                     num_kv_heads, head_size, q_stride, k_stride, cs, rot_dim, max_position);
     };
-    err = !neox ? go(rope_vec_kernel<T, C, false, false>)
-                : (sm ? go(rope_vec_kernel<T, C, true, true>) : go(rope_vec_kernel<T, C, true, false>));
+    const bool tight = split > 1 && num_tokens > 128;
+    err = !neox ? go(rope_vec_kernel<T, C, false, false, false>)
+          : sm  ? go(rope_vec_kernel<T, C, true, true, false>)
+          : tight ? go(rope_vec_kernel<T, C, true, false, true>)
+                  : go(rope_vec_kernel<T, C, true, false, false>);
   } else {
     err = neox ? launch(rope_scalar_kernel<T, C, true>, grid, dim3(256), 0, stream, positions, q,
                         k, num_heads, num_kv_heads, head_size, q_stride, k_stride, cs, rot_dim,
