@@ -220,12 +220,13 @@ int launch_rope(const int64_t* positions, void* query, void* key, int64_t num_to
   if (vec) {
     const int uph = neox ? embed / V : rot_dim / V;
     const int64_t units = (int64_t)(num_heads + num_kv_heads) * uph;
-    // NeoX: a token's units (one per thread) may be split over gridDim.y CTAs.
+    // NeoX: a token's units (one per thread) may be split over several CTAs.
     // Measured on B200 (Llama-3-8B, 320 units): 2-warp CTAs are fastest for
     // decode-sized batches (T <= 128: 13-18 % over one CTA per token), one CTA
-    // per token at T ~ 512, 5-warp CTAs for long prefills (T > 1024: 9 %).
+    // per token up to T = 512, 5-warp CTAs above (T = 768-1024: 12-14 %; long
+    // prefills: 9 %).
     int64_t per_cta = 512;
-    if (neox) per_cta = num_tokens <= 128 ? 64 : (num_tokens > 1024 ? 160 : 512);
+    if (neox) per_cta = num_tokens <= 128 ? 64 : (num_tokens > 512 ? 160 : 512);
     int64_t split = neox ? ceil_div(units, per_cta) : 1;
     if (split > 65535) split = 1;  // grid.y limit: one CTA per token loops over the units
     int threads = (int)ceil_div(ceil_div(units, split), 32) * 32;
