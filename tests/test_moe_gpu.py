@@ -160,6 +160,22 @@ def test_moe_align_large_inputs(numel, E, bs, fill):
     np.testing.assert_array_equal(e[: t // bs], oe)
 
 
+@pytest.mark.parametrize("numel", [2, 31, 32, 33, 200, 255, 256, 257])
+@pytest.mark.parametrize("E,bs", [(1, 16), (8, 64), (32, 4), (7, 3)])
+@pytest.mark.parametrize("fill", [False, True])
+def test_moe_align_small_sizes(numel, E, bs, fill):
+    """Decode-sized inputs around warp multiples, ids outside [0, E) mixed in,
+    with and without in-kernel padding."""
+    rng = np.random.default_rng(numel * 31 + E)
+    ids = rng.integers(-1, E + 1, size=numel)
+    t_ids = torch.from_numpy(ids).to(torch.int32)
+    s, e, t = run_align(t_ids, E, bs, fill_padding=fill, prefill=None if not fill else -3)
+    os_, oe, ot = moe_ref.moe_align_block_size_c(ids, E, bs)
+    assert t == ot
+    np.testing.assert_array_equal(s, os_)
+    np.testing.assert_array_equal(e[: t // bs], oe)
+
+
 def test_moe_align_fill_padding_and_invalid_ids():
     ids = torch.tensor([0, 9, 1, -1, 1, 3, 3, 3], dtype=torch.int64)
     s, e, t = run_align(ids, 4, 2, fill_padding=True, prefill=-5)
