@@ -12,8 +12,10 @@
 //    rounded where the reference's T-typed arithmetic rounds
 //    (csrc/activation_kernels.cu:86-98).
 //
-// Design: pure streaming.  2-D grid (row, column chunk); each thread loads its
-// 16-byte vector of both input halves before any math and stores one vector.
+// Design: pure streaming.  2-D grid of (column chunk, row) -- chunk-major, so
+// CTAs dispatched together stream neighbouring pieces of one row; each thread
+// loads its 16-byte vector of both input halves before any math and stores one
+// vector.
 // Unaligned shapes use a scalar kernel with the same arithmetic.
 #include "common.cuh"
 

@@ -7,11 +7,12 @@
 // restates the PyTorch composition at paceserve/model_executor/models/llama.py:
 // 248-252: residual <- (T)(x + residual), then rms_norm of that rounded sum.
 //
-// Design: one CTA per token row; the row is read once with 16-byte vectors and
-// held in registers across the reduction (the reference reads it twice with
-// 2-byte loads); warp-shuffle then shared-memory reduction, fixed order so all
-// threads derive the identical inv.  Rows that do not meet the vector
-// alignment go through a scalar two-pass kernel.
+// Design: one CTA per token row (two rows for the plain norm at large T); the
+// row is read once with 16-byte vectors and held in registers across the
+// reduction (the reference reads it twice with 2-byte loads); warp-shuffle
+// then shared-memory reduction, fixed order so all threads derive the
+// identical inv.  Rows that do not meet the vector alignment go through a
+// scalar two-pass kernel.
 #include "common.cuh"
 
 namespace pace {

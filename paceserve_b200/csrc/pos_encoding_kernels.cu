@@ -10,10 +10,12 @@
 // may be fp32 while q/k are bf16/fp16, and a token whose position is outside
 // [0, max_position) is left unchanged instead of reading outside the cache.
 //
-// Design: one CTA per token; a thread owns one "unit" of one head: for NeoX a
-// 16-byte vector of the first half plus the matching vector of the second
-// half, for GPT-J one 16-byte vector of interleaved pairs, so every q/k access
-// is a coalesced 16-byte load/store and cos/sin are fetched as vectors too.
+// Design: a thread owns one "unit" of one head: for NeoX a 16-byte vector of
+// the first half plus the matching vector of the second half, for GPT-J one
+// 16-byte vector of interleaved pairs, so every q/k access is a coalesced
+// 16-byte load/store and cos/sin are fetched as vectors too.  A token's units
+// are covered by one CTA, or (NeoX) split over several CTAs whose size depends
+// on the batch (see launch_rope).
 #include "common.cuh"
 
 namespace pace {
