@@ -477,6 +477,58 @@ def kv_host_path(sc, dc, sids, dids, steps, warmup):
             "round_trip_gbs": round(nbytes / ((ms_g + ms_s) * 1e-3) / 1e9, 2)}
 
 
+def kv_overlap(dev, reps: int = 100):
+    """Promotion while serving, on one GPU: the 32-layer chain (a CUDA graph) on
+    the main stream and the promotion copy (1.1 GB, HBM -> HBM) on a side
+    stream at the same time.  Per copy method: the chain's ms per step and the
+    copy's GB/s, alone and concurrent, and the HBM bytes both moved per second."""
+    import torch
+
+    import paceserve_b200 as pb
+    from paceserve_b200 import kv_transfer as kvt
+
+    ops = (pb.layernorm_ops, pb.pos_encoding_ops, pb.activation_ops)
+    ch = build_chain(dev, seed=5)
+    g = capture(lambda: run_chain(ch, ops))
+    _, src, dst = kv_requests(7)
+    sc = _kv_caches(dev, fill_seed=100)
+    dc = _kv_caches(dev)
+    sids = torch.tensor(src, dtype=torch.int32, device=dev)
+    dids = torch.tensor(dst, dtype=torch.int32, device=dev)
+    nbytes = len(src) * KV_L * KV_BLOCK_BYTES
+    chain_ms = time_replays(g, reps, 5) / reps
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    out = {"chain_ms_alone": round(chain_ms, 4), "copy_bytes": nbytes}
+    for m, name in KV_METHODS.items():
+        copy = lambda: kvt.promote(sc, dc, sids, dids, method=m)  # noqa: E731
+        copy_ms = _time_copy(copy, 20, 3)
+        n_copy = max(1, round(reps * chain_ms / copy_ms))
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(main)
+        ev[2].record(side)
+        for i in range(max(reps, n_copy)):
+            if i < reps:
+                g.replay()
+            if i < n_copy:
+                with torch.cuda.stream(side):
+                    copy()
+        ev[1].record(main)
+        ev[3].record(side)
+        torch.cuda.synchronize()
+        c_ms = ev[0].elapsed_time(ev[1]) / reps
+        k_ms = ev[2].elapsed_time(ev[3]) / n_copy
+        span = max(ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])) * 1e-3
+        out[name] = {"copy_gbs_alone": round(nbytes / (copy_ms * 1e-3) / 1e9, 1),
+                     "chain_ms_concurrent": round(c_ms, 4),
+                     "chain_slowdown": round(c_ms / chain_ms - 1, 4),
+                     "copy_gbs_concurrent": round(nbytes / (k_ms * 1e-3) / 1e9, 1),
+                     "hbm_gbs_both": round((reps * B_STEP + 2 * n_copy * nbytes) / span / 1e9, 1)}
+    del g
+    return out
+
+
 def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
     """LP->HP promotion on rank pairs (0->1, 2->3, ...): the HP rank pulls the
     request blocks from the LP rank's caches (CUDA IPC) with one kernel.  With one
@@ -764,6 +816,9 @@ def run_side_workload(args, ws, rank, local):
         if rank == 0:
             torch.cuda.empty_cache()
             line["kv_append"] = append_bench(dev)
+            if ws == 1:
+                torch.cuda.empty_cache()
+                line["kv_overlap"] = kv_overlap(dev)
     elif args.workload == "sweep":
         line = {"metric": "per-op HBM GB/s, token sweep", "sweep": sweep(dev) if rank == 0 else None,
                 "peak_gbs": peaks()["hbm_gbs"]}
