@@ -478,59 +478,73 @@ def kv_host_path(sc, dc, sids, dids, steps, warmup):
             "round_trip_gbs": round(nbytes / ((ms_g + ms_s) * 1e-3) / 1e9, 2)}
 
 
-def kv_overlap(dev, reps: int = 100):
-    """Promotion while serving, on one GPU: the 32-layer chain (a CUDA graph) on
-    the main stream and the promotion copy (1.1 GB, HBM -> HBM) on a side
-    stream at the same time.  Per copy method: the chain's ms per step and the
-    copy's GB/s, alone and concurrent, and the HBM bytes both moved per second."""
+def _overlap_one(g, chain_ms, copy, nbytes, reps):
+    """The chain graph `g` on the current stream and `copy` on a side stream,
+    launched interleaved so both run for about the same time."""
     import torch
 
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        copy_ms = _time_copy(copy, 10, 3)
+    n_copy = max(1, round(reps * chain_ms / copy_ms))
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record(main)
+    ev[2].record(side)
+    for i in range(max(reps, n_copy)):
+        if i < reps:
+            g.replay()
+        if i < n_copy:
+            with torch.cuda.stream(side):
+                copy()
+    ev[1].record(main)
+    ev[3].record(side)
+    torch.cuda.synchronize()
+    c_ms = ev[0].elapsed_time(ev[1]) / reps
+    k_ms = ev[2].elapsed_time(ev[3]) / n_copy
+    return {"copy_gbs_alone": round(nbytes / (copy_ms * 1e-3) / 1e9, 1),
+            "chain_ms_concurrent": round(c_ms, 4),
+            "chain_slowdown": round(c_ms / chain_ms - 1, 4),
+            "copy_gbs_concurrent": round(nbytes / (k_ms * 1e-3) / 1e9, 1)}
+
+
+def _overlap_chain(dev, copies, nbytes, reps):
+    """Chain alone, then beside each copy in `copies` ({name: callable})."""
     import paceserve_b200 as pb
-    from paceserve_b200 import kv_transfer as kvt
 
     ops = (pb.layernorm_ops, pb.pos_encoding_ops, pb.activation_ops)
     ch = build_chain(dev, seed=5)
     g = capture(lambda: run_chain(ch, ops))
+    chain_ms = time_replays(g, reps, 5) / reps
+    out = {"chain_ms_alone": round(chain_ms, 4), "copy_bytes": nbytes}
+    for name, copy in copies.items():
+        out[name] = _overlap_one(g, chain_ms, copy, nbytes, reps)
+    del g
+    return out
+
+
+def kv_overlap(dev, reps: int = 100):
+    """Promotion while serving, on one GPU: the 32-layer chain (a CUDA graph) on
+    the main stream and the promotion copy (1.1 GB, HBM -> HBM) on a side
+    stream at the same time.  Per copy method: the chain's ms per step and the
+    copy's GB/s, alone and concurrent."""
+    import torch
+
+    from paceserve_b200 import kv_transfer as kvt
+
     _, src, dst = kv_requests(7)
     sc = _kv_caches(dev, fill_seed=100)
     dc = _kv_caches(dev)
     sids = torch.tensor(src, dtype=torch.int32, device=dev)
     dids = torch.tensor(dst, dtype=torch.int32, device=dev)
     nbytes = len(src) * KV_L * KV_BLOCK_BYTES
-    chain_ms = time_replays(g, reps, 5) / reps
-    main = torch.cuda.current_stream()
-    side = torch.cuda.Stream()
-    out = {"chain_ms_alone": round(chain_ms, 4), "copy_bytes": nbytes}
-    for m, name in KV_METHODS.items():
-        copy = lambda: kvt.promote(sc, dc, sids, dids, method=m)  # noqa: E731
-        copy_ms = _time_copy(copy, 20, 3)
-        n_copy = max(1, round(reps * chain_ms / copy_ms))
-        torch.cuda.synchronize()
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        ev[0].record(main)
-        ev[2].record(side)
-        for i in range(max(reps, n_copy)):
-            if i < reps:
-                g.replay()
-            if i < n_copy:
-                with torch.cuda.stream(side):
-                    copy()
-        ev[1].record(main)
-        ev[3].record(side)
-        torch.cuda.synchronize()
-        c_ms = ev[0].elapsed_time(ev[1]) / reps
-        k_ms = ev[2].elapsed_time(ev[3]) / n_copy
-        span = max(ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])) * 1e-3
-        out[name] = {"copy_gbs_alone": round(nbytes / (copy_ms * 1e-3) / 1e9, 1),
-                     "chain_ms_concurrent": round(c_ms, 4),
-                     "chain_slowdown": round(c_ms / chain_ms - 1, 4),
-                     "copy_gbs_concurrent": round(nbytes / (k_ms * 1e-3) / 1e9, 1),
-                     "hbm_gbs_both": round((reps * B_STEP + 2 * n_copy * nbytes) / span / 1e9, 1)}
-    del g
-    return out
+    copies = {name: (lambda m=m: kvt.promote(sc, dc, sids, dids, method=m))
+              for m, name in KV_METHODS.items()}
+    return _overlap_chain(dev, copies, nbytes, reps)
 
 
-def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
+def kv_promotion(ws, rank, local, steps, warmup, baseline=True, overlap=False):
     """LP->HP promotion on rank pairs (0->1, 2->3, ...): the HP rank pulls the
     request blocks from the LP rank's caches (CUDA IPC) with one kernel.  With one
     GPU, LP and HP caches both live on it (an HBM-to-HBM copy).  Returns the
@@ -604,9 +618,15 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
         dist.recv(g, src=mine[1])
         ok = bool(torch.equal(torch.stack([c[dids.long()] for c in caches]), g))
         del g
+        if overlap:
+            # Promotion while serving: the HP GPU runs the chain while pulling.
+            copies = {name: (lambda m=m: kvt.promote(imported, caches, sids, dids, method=m))
+                      for m, name in KV_METHODS.items()}
+            out_overlap = _overlap_chain(dev, copies, nbytes, 60)
         imported.close()
     info = [None] * ws
-    dist.all_gather_object(info, (role, ok, nbytes, [times[m] for m in KV_METHODS]))
+    ov = out_overlap if (overlap and role == "hp") else None
+    dist.all_gather_object(info, (role, ok, nbytes, [times[m] for m in KV_METHODS], ov))
     dist.barrier()
     hps = [x for x in info if x[0] == "hp"]
     total = sum(x[2] for x in hps)
@@ -624,6 +644,8 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True):
                 "byte_exact": all(x[1] for x in info), "methods": res,
                 "nvlink_frac": round(best["gbs_per_pair"] / NVLINK_GBS, 4),
                 "nvlink_peak_gbs": NVLINK_GBS, "nvlink_peak_source": "measured peer copy on this pool"})
+    if overlap:
+        out["overlap_on_hp"] = [x[4] for x in hps]
     return out
 
 
@@ -812,7 +834,7 @@ def run_side_workload(args, ws, rank, local):
     torch.cuda.set_device(dev)
     if args.workload == "kv":
         res = kv_promotion(ws, rank, local, steps=min(args.steps, 50), warmup=args.warmup,
-                           baseline=not args.no_cpu_baseline)
+                           baseline=not args.no_cpu_baseline, overlap=ws > 1)
         line = {"metric": "LP->HP KV-promotion GB/s", "n_gpus": ws, "kv_promotion": res}
         if rank == 0:
             torch.cuda.empty_cache()
