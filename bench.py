@@ -679,10 +679,13 @@ def append_bench(dev, reps: int = 20):
     import paceserve_b200 as pb
 
     num_pages = 4096
+    layers = L if KV_NB >= 8192 else 4  # the small --kv-blocks case (for ncu) keeps 1 GiB
     ai, kp, ki, kl = (x.to(dev) for x in append_metadata(num_pages=num_pages))
     g = torch.Generator(device=dev).manual_seed(5)
-    caches = [torch.zeros(num_pages, 2, 16, NKV, HD, dtype=torch.bfloat16, device=dev) for _ in range(L)]
-    qkvs = [torch.randn(T, (NQ + 2 * NKV) * HD, generator=g, device=dev).bfloat16() for _ in range(L)]
+    caches = [torch.zeros(num_pages, 2, 16, NKV, HD, dtype=torch.bfloat16, device=dev)
+              for _ in range(layers)]
+    qkvs = [torch.randn(T, (NQ + 2 * NKV) * HD, generator=g, device=dev).bfloat16()
+            for _ in range(layers)]
     kv = pb.kv_transfer_ops
 
     def fn():
@@ -690,7 +693,7 @@ def append_bench(dev, reps: int = 20):
             kv.append_paged_kv_cache_by_indptr(q[:, NQ * HD:(NQ + NKV) * HD], q[:, (NQ + NKV) * HD:],
                                                ai, c, ki, kp, kl)
     gr = capture(fn)
-    us = time_replays(gr, reps, 3) * 1e3 / (reps * L)
+    us = time_replays(gr, reps, 3) * 1e3 / (reps * layers)
     nbytes = 2 * 2 * T * NKV * HD * 2  # read K and V rows, write them into the pages
     return {"us_per_layer": round(us, 3), "bytes_per_layer": nbytes,
             "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
