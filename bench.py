@@ -168,11 +168,15 @@ def rope_cache(device, max_pos: int = MAX_POS):
     return torch.cat([f.cos(), f.sin()], -1).float().to(device)
 
 
-def build_chain(device, seed=0):
+def build_chain(device, seed=0, tokens=None):
+    """The 32 layers' buffers.  tokens=None: the Sarathi batch (448 prefill + 64
+    decode tokens); otherwise a pure decode batch of `tokens` tokens at
+    positions uniform in [1, MAX_POS)."""
     import torch
 
     gen = torch.Generator(device=device).manual_seed(seed)
     cpu_gen = torch.Generator().manual_seed(seed)
+    T = tokens or globals()["T"]
 
     def rn(*shape, mean=0.0, std=1.0):
         return (torch.randn(*shape, generator=gen, device=device) * std + mean).to(torch.bfloat16)
@@ -196,7 +200,11 @@ def build_chain(device, seed=0):
         b["q"] = b["qkv"][:, : NQ * HD]
         b["k"] = b["qkv"][:, NQ * HD: (NQ + NKV) * HD]
         layers.append(b)
-    return {"layers": layers, "positions": make_positions(cpu_gen, device), "cache": rope_cache(device)}
+    if tokens:
+        pos = torch.randint(1, MAX_POS, (T,), generator=cpu_gen, dtype=torch.int64).to(device)
+    else:
+        pos = make_positions(cpu_gen, device)
+    return {"layers": layers, "positions": pos, "cache": rope_cache(device), "tokens": T}
 
 
 def run_chain(ch, ops) -> None:

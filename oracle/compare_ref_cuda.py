@@ -66,6 +66,36 @@ def main():
         ms = bench.time_replays(g, args.reps, 5) / args.reps
         res[name] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(bench.T / (ms * 1e-3), 1)}
         del g
+    # Decode-sized batches: the same 32-layer chain at T = 1, 16 and 64 decode tokens.
+    decode = []
+    for t in (1, 16, 64):
+        dch = bench.build_chain(dev, seed=8, tokens=t)
+        dl, dpos = dch["layers"], dch["positions"]
+        for b in dl:
+            b.setdefault("normed", torch.empty(t, H, dtype=torch.bfloat16, device=dev))
+            b["res_sum"] = torch.empty(t, H, dtype=torch.bfloat16, device=dev)
+
+        def ref_decode():
+            for l, b in enumerate(dl):
+                if l == 0:
+                    ln_r.rms_norm(b["normed"], b["hidden"], b["w_in"], EPS)
+                else:
+                    torch.add(b["hidden"], b["residual"], out=b["res_sum"])
+                    ln_r.rms_norm(b["normed"], b["res_sum"], b["w_in"], EPS)
+                pe_r.rotary_embedding(dpos, b["q"], b["k"], HD, cache_bf16, True)
+                torch.add(b["attn"], b["residual2"], out=b["res_sum"])
+                ln_r.rms_norm(b["normed"], b["res_sum"], b["w_post"], EPS)
+                act_r.silu_and_mul(b["act"], b["gate_up"])
+
+        row = {"T": t}
+        for name, fn in (("ours", lambda: bench.run_chain(dch, ours)), ("reference_cuda", ref_decode)):
+            g = bench.capture(fn)
+            row[name + "_us_per_step"] = round(bench.time_replays(g, args.reps, 5) * 1e3 / args.reps, 2)
+            del g
+        row["speedup"] = round(row["reference_cuda_us_per_step"] / row["ours_us_per_step"], 2)
+        decode.append(row)
+        del dch
+    res["decode_chain"] = decode
     single = {
         "rms_norm": (lambda: [ln_r.rms_norm(b["normed"], b["hidden"], b["w_in"], EPS) for b in lay],
                      lambda: [pb.layernorm_ops.rms_norm(b["normed"], b["hidden"], b["w_in"], EPS) for b in lay],
