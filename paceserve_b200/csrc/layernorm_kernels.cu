@@ -254,11 +254,14 @@ int launch_norm(const void* x_in, void* x_out, void* res, const void* weight, fl
   cudaError_t err;
   const dim3 grid((unsigned)num_tokens);
   if (vec) {
-    // Threads per row, measured on B200: the fused norm up to 512; the plain
-    // norm up to 256, and 128 for 1024 <= T < 8192 (4 vectors per thread at
-    // H = 4096: 8-15 % faster there, 0-13 % slower below).
+    // Threads per row, measured on B200: the fused norm up to 512, but 256 for
+    // T <= 128 with rows of <= 512 vectors (H = 4096 bf16: 20 % faster at
+    // T = 128, 1-3 % below; wider rows were 3 % slower); the plain norm up to
+    // 256, and 128 for 1024 <= T < 8192 (4 vectors per thread at H = 4096: 8-15 %
+    // faster there, 0-13 % slower below).
     const int max_threads =
-        FUSED ? kMaxThreads : (num_tokens >= 1024 && num_tokens < 8192 ? 128 : kMaxThreads / 2);
+        FUSED ? (num_tokens <= 128 && nvec <= 512 ? 256 : kMaxThreads)
+              : (num_tokens >= 1024 && num_tokens < 8192 ? 128 : kMaxThreads / 2);
     int nv = 1;
     while (nv < 4 && ceil_div(nvec, nv) > max_threads) nv *= 2;
     int threads = (int)ceil_div(ceil_div(nvec, nv), 32) * 32;

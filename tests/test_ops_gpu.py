@@ -73,7 +73,8 @@ def test_rms_norm_empty_and_strided():
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("T,H", [(1, 4096), (17, 4096), (512, 4096), (33, 8192), (6, 200)])
+@pytest.mark.parametrize("T,H", [(1, 4096), (17, 4096), (128, 4096), (129, 4096), (512, 4096),
+                                 (33, 8192), (6, 200)])
 def test_fused_add_rms_norm(T, H, dtype):
     x = randn(T, H, dtype=dtype, seed=T + H)
     r = randn(T, H, dtype=dtype, seed=T + H + 1)
