@@ -198,11 +198,14 @@ int launch_act(void* out, const void* in, int64_t num_tokens, int64_t d, int64_t
     // 512-thread CTAs were 3-15 % slower).  Chunk-major order (consecutive CTAs
     // on consecutive pieces of the same row) is 3-4 % faster than row-major
     // at every T >= 512; rows beyond the grid's y limit use row-major.
-    const int64_t chunks = ceil_div(nvec, 256);
+    // Decode batches (T <= 128) use 128-thread CTAs: twice the CTAs spread the
+    // few rows over more SMs (T = 1: 10 % faster).
+    const int threads = num_tokens <= 128 ? 128 : 256;
+    const int64_t chunks = ceil_div(nvec, threads);
     const bool cm = num_tokens <= 65535;
     const dim3 grid = cm ? dim3((unsigned)chunks, (unsigned)num_tokens)
                          : dim3((unsigned)num_tokens, (unsigned)chunks);
-    err = launch(act_vec_kernel<T, Op, 1, GATED>, grid, dim3(256), 0, stream, o, x, d,
+    err = launch(act_vec_kernel<T, Op, 1, GATED>, grid, dim3(threads), 0, stream, o, x, d,
                  in_stride, out_stride, cm ? 1 : 0);
   } else {
     const int64_t bx = ceil_div(d, 256) < 64 ? ceil_div(d, 256) : 64;
@@ -220,7 +223,9 @@ int act_entry(void* out, const void* input, int64_t num_tokens, int64_t d, int64
   if (num_tokens < 0 || d < 0 || num_tokens > INT32_MAX)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad shape [%lld, %lld]", name,
                 (long long)num_tokens, (long long)d);
-  if (d / 8 > 65535LL * 256)
+  // Past 65535 rows the grid is row-major, with the row's chunks (256 x 4
+  // fp32 elements at least) in grid.y.
+  if (num_tokens > 65535 && d / 4 > 65535LL * 256)
     return fail(PACE_ERR_TOO_LARGE, "%s: row width %lld too large", name, (long long)d);
   const int64_t in_w = GATED ? 2 * d : d;
   if (in_stride < in_w || out_stride < d)
