@@ -198,9 +198,10 @@ int launch_act(void* out, const void* in, int64_t num_tokens, int64_t d, int64_t
     // 512-thread CTAs were 3-15 % slower).  Chunk-major order (consecutive CTAs
     // on consecutive pieces of the same row) is 3-4 % faster than row-major
     // at every T >= 512; rows beyond the grid's y limit use row-major.
-    // Decode batches (T <= 128) use 128-thread CTAs: twice the CTAs spread the
-    // few rows over more SMs (T = 1: 10 % faster).
-    const int threads = num_tokens <= 128 ? 128 : 256;
+    // Decode batches (T <= 64) use 128-thread CTAs: twice the CTAs spread the
+    // few rows over more SMs (T = 1: 12 % faster; at T = 128 the 70B width was
+    // 8 % slower).
+    const int threads = num_tokens <= 64 ? 128 : 256;
     const int64_t chunks = ceil_div(nvec, threads);
     const bool cm = num_tokens <= 65535;
     const dim3 grid = cm ? dim3((unsigned)chunks, (unsigned)num_tokens)
