@@ -97,13 +97,16 @@ def export_caches(caches: Sequence[torch.Tensor]) -> CacheExport:
     if not caches:
         raise ValueError("no caches to export")
     handles, offsets = [], []
+    c0 = caches[0]
     for c in caches:
         if not (c.is_cuda and c.is_contiguous()):
             raise ValueError("caches must be contiguous CUDA tensors")
+        if c.shape != c0.shape or c.dtype != c0.dtype or c.device != c0.device:
+            raise ValueError("every layer's cache must share the first layer's shape, dtype "
+                             "and device")
         h, off = kv_ops.ipc_get_handle(c)
         handles.append(bytes(h))
         offsets.append(int(off))
-    c0 = caches[0]
     return CacheExport(handles, offsets, int(c0.shape[0]),
                        int(c0[0].numel() * c0.element_size()) if c0.shape[0] else 0,
                        int(c0.device.index), tuple(c0.shape), str(c0.dtype))
@@ -133,10 +136,14 @@ class ImportedCaches:
         return self.export.num_blocks
 
     def close(self) -> None:
-        for b in self._bases:
+        """Unmap the peer's caches (idempotent).  Synchronises this device first,
+        so no copy still reading the mapping is in flight when it goes away.
+        Not done implicitly on garbage collection, for the same reason."""
+        bases, self._bases, self.ptrs = self._bases, [], []
+        if bases:
+            torch.cuda.synchronize(self.device)
+        for b in bases:
             kv_ops.ipc_close_handle(b)
-        self._bases = []
-        self.ptrs = []
 
     def __enter__(self):
         return self
