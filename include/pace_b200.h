@@ -238,7 +238,9 @@ int pace_ipc_get_handle(const void* dev_ptr, void* handle_out, int64_t* offset_o
 /* Map an exported allocation into this process on `device`; *base_out is the
  * allocation's base (add the exporter's offset). */
 int pace_ipc_open_handle(const void* handle, int device, void** base_out);
-/* Unmap a base returned by pace_ipc_open_handle. */
+/* Unmap a base returned by pace_ipc_open_handle.  The caller must first make
+ * sure no launched copy still reads or writes the mapping (synchronise the
+ * streams that used it). */
 int pace_ipc_close_handle(void* base);
 
 #ifdef __cplusplus
