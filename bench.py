@@ -288,26 +288,48 @@ def per_op_times(ch, ops, reps=20):
     return out
 
 
-def e2e_chain(ch, ops, steps, warmup, ws=1):
-    """Public-API path: pinned host inputs -> device, eager op calls, device -> host output.
-    With ws > 1 every rank runs it between barriers; the time is the max over ranks
-    and the value the whole job's tokens/s."""
+def e2e_chain(chs, ops, steps, warmup, ws=1):
+    """Public-API path, pipelined the way a serving engine runs it: step i uses chain
+    state i % 2 (`chs` holds two); its inputs go host -> device on an H2D stream
+    from page-locked memory, the ops run eagerly (pybind -> C ABI) on the compute
+    stream, and its output goes device -> host on a D2H stream, so the copies of
+    one step overlap the ops of the next.  Events order every reuse of a buffer.
+    Every step's copies lie inside the timed region.  With ws > 1 every rank runs
+    it between barriers; the time is the max over ranks and the value the whole
+    job's tokens/s."""
     import torch
 
-    dev = ch["positions"].device
-    h_pos = ch["positions"].cpu().pin_memory()
-    h_hidden = ch["layers"][0]["hidden"].cpu().pin_memory()
-    h_out = torch.empty(T, I, dtype=torch.bfloat16, pin_memory=True)
-    out_dev = ch["layers"][-1]["act"]
+    dev = chs[0]["positions"].device
+    comp = torch.cuda.current_stream()
+    h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
+    h_pos = [c["positions"].cpu().pin_memory() for c in chs]
+    h_hidden = [c["layers"][0]["hidden"].cpu().pin_memory() for c in chs]
+    h_out = [torch.empty(T, I, dtype=torch.bfloat16, pin_memory=True) for _ in chs]
+    comp_done = [torch.cuda.Event() for _ in chs]
+    d2h_done = [torch.cuda.Event() for _ in chs]
+    for e in comp_done + d2h_done:
+        e.record(comp)
 
-    def step():
-        ch["positions"].copy_(h_pos, non_blocking=True)
-        ch["layers"][0]["hidden"].copy_(h_hidden, non_blocking=True)
+    def step(i):
+        k = i % len(chs)
+        ch = chs[k]
+        h2d_done = torch.cuda.Event()
+        with torch.cuda.stream(h2d_s):
+            h2d_s.wait_event(comp_done[k])  # the previous step on this state read its inputs
+            ch["positions"].copy_(h_pos[k], non_blocking=True)
+            ch["layers"][0]["hidden"].copy_(h_hidden[k], non_blocking=True)
+            h2d_done.record(h2d_s)
+        comp.wait_event(h2d_done)
+        comp.wait_event(d2h_done[k])  # ... and its output has been copied out
         run_chain(ch, ops)
-        h_out.copy_(out_dev, non_blocking=True)
+        comp_done[k].record(comp)
+        with torch.cuda.stream(d2h_s):
+            d2h_s.wait_event(comp_done[k])
+            h_out[k].copy_(ch["layers"][-1]["act"], non_blocking=True)
+            d2h_done[k].record(d2h_s)
 
-    for _ in range(warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize(dev)
     if ws > 1:
         import torch.distributed as dist
@@ -316,10 +338,14 @@ def e2e_chain(ch, ops, steps, warmup, ws=1):
         torch.cuda.synchronize(dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
+    e0.record(comp)
+    h2d_s.wait_event(e0)
+    d2h_s.wait_event(e0)
+    for i in range(steps):
+        step(i)
+    for e in d2h_done:
+        comp.wait_event(e)
+    e1.record(comp)
     e1.synchronize()
     ms = e0.elapsed_time(e1) / steps
     if ws > 1:
@@ -327,9 +353,12 @@ def e2e_chain(ch, ops, steps, warmup, ws=1):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
     return {"value": round(ws * T / (ms * 1e-3), 1), "unit": UNIT,
-            "h2d_bytes_per_step": h_pos.numel() * 8 + h_hidden.numel() * 2,
-            "d2h_bytes_per_step": h_out.numel() * 2, "ms_per_step": round(ms, 4),
-            "steps": steps, "path": "eager calls of paceserve_b200 ops (pybind -> C ABI)"}
+            "h2d_bytes_per_step": h_pos[0].numel() * 8 + h_hidden[0].numel() * 2,
+            "d2h_bytes_per_step": h_out[0].numel() * 2, "ms_per_step": round(ms, 4),
+            "steps": steps,
+            "path": "eager calls of paceserve_b200 ops (pybind -> C ABI); inputs in and the "
+                    "last layer's output out every step, on copy streams overlapping the "
+                    "next step's ops"}
 
 
 # ------------------------------------------------------------ CPU oracle --
@@ -929,7 +958,8 @@ def main():
             "frac_of_nominal": round(silu["gbs"] / NOMINAL_HBM_GBS, 4),
             "traffic": ncu_traffic("silu_and_mul_T512"),
             "algorithmic_bytes": B_SILU}
-    e2e = e2e_chain(ch, ops, steps=min(args.steps, 50), warmup=3, ws=ws)
+    e2e = e2e_chain([ch, build_chain(dev, seed=4321 + rank)], ops, steps=min(args.steps, 50),
+                    warmup=3, ws=ws)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
