@@ -14,8 +14,9 @@ drives nvcc/g++ with torch's include paths, which is how torch's
 The resulting ``.so`` files are git-ignored but travel to the GPU box, where
 ``load_ref_ops`` imports them without the reference sources being present.
 
-Usage: ``python oracle/build_ref.py [reference_root]`` (default
-``/root/reference``).  Skips modules whose ``.so`` is newer than its sources.
+Usage: ``python oracle/build_ref.py [reference_root]`` (default: the
+``PACE_REFERENCE_ROOT`` environment variable, else ``DEFAULT_REF_ROOT``).
+Skips modules whose ``.so`` is newer than its sources.
 """
 from __future__ import annotations
 
@@ -27,6 +28,7 @@ from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, "_ref")
+DEFAULT_REF_ROOT = os.environ.get("PACE_REFERENCE_ROOT", "/root/reference")
 
 # module name -> reference source files (paths relative to the reference root)
 REF_MODULES = {
@@ -76,7 +78,7 @@ def _build_one(name: str, ref_root: str, verbose: bool) -> str:
     return out
 
 
-def build(ref_root: str = "/root/reference", verbose: bool = False, jobs: int = 4) -> list[str]:
+def build(ref_root: str = DEFAULT_REF_ROOT, verbose: bool = False, jobs: int = 4) -> list[str]:
     """Compile every reference module missing or stale under ``oracle/_ref``."""
     if not os.path.isdir(os.path.join(ref_root, "csrc")):
         return []
@@ -106,6 +108,6 @@ def load_ref_ops(name: str):
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF_ROOT
     for p in build(root, verbose=True):
         print("built", p)
