@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of PaceServe's per-layer op chain on B200.
+"""Benchmark of PaceServe's per-layer op chain on B200 (the headline workload).
 
 One step = one pass of the Llama-3-8B 32-layer op sequence over one Sarathi
 mixed batch of T=512 tokens (a 448-token prefill chunk at positions 0..447 plus
@@ -401,7 +401,7 @@ def cpu_chain_sample(budget_s: float = 8.0, max_passes: int = 1 << 30, warmup: i
 
 
 def cpu_config1_sample(budget_s: float = 3.0):
-    """BASELINE config 1 on the host cores: one Llama-3-8B layer's ops in fp32 at
+    """The CPU-runnable workload on the host cores: one Llama-3-8B layer's ops in fp32 at
     T=64 (fused_add_rms_norm -> neox rope -> silu_and_mul), the oracle's torch
     formulas; wall time per chain and fp32 algorithmic bytes per second."""
     import torch
@@ -420,7 +420,7 @@ def cpu_config1_sample(budget_s: float = 3.0):
         n += 1
     ms = t_sum / n * 1e3
     nbytes = ops_ref.CONFIG1["T"] * ops_ref.CONFIG1_BYTES_PER_TOKEN
-    return {"workload": "config 1: one Llama-3-8B layer, fp32, T=64 (fused_add_rms_norm, neox "
+    return {"workload": "one Llama-3-8B layer, fp32, T=64 (fused_add_rms_norm, neox "
                         "rope q[64,32,128] k[64,8,128], silu_and_mul [64,28672])",
             "ms_per_chain": round(ms, 3), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
             "tokens_per_s": round(ops_ref.CONFIG1["T"] / (ms * 1e-3), 1), "cores": cores,
@@ -434,7 +434,7 @@ KV_METHODS = {1: "simt", 2: "bulk"}
 
 
 def kv_requests(seed: int):
-    """8 promoted requests, prompt lengths
+    """The promotion workload: 8 promoted requests, prompt lengths
     min(8192, round(lognormal(6.9, 0.7))) -> ceil(len/16) blocks each, taken from
     random occupied blocks of an 80 %-full LP cache and scattered into random free
     blocks of an HP cache that is 80 % full with other requests."""
@@ -743,7 +743,7 @@ NVLINK_GBS = 770.0  # measured peer copy per direction on this pool (900 nominal
 
 # ------------------------------------------------------------ sweep / MoE --
 def sweep(dev, reps=10):
-    """per-op GB/s for T in {1..16384}, Llama-3-8B and -70B shapes,
+    """Token sweep: per-op GB/s for T in {1..16384}, Llama-3-8B and -70B shapes,
     bf16 and fp16.  Each op is timed as a CUDA graph over enough distinct buffers
     that every launch reads cold data (working set >= 512 MB per cycle)."""
     import torch
@@ -788,7 +788,7 @@ def sweep(dev, reps=10):
 
 
 def moe_routing(dev, reps=50):
-    """topk_softmax (E=8, top-2, renormalised) then
+    """Mixtral-8x7B routing: topk_softmax (E=8, top-2, renormalised) then
     moe_align_block_size (block 64) on N(0,1) fp32 gating logits."""
     import numpy as np
     import torch
@@ -907,8 +907,8 @@ def main():
     ap.add_argument("--kv-blocks", type=int, default=8192,
                     help="blocks per layer of the kv workload's caches (a smaller case for ncu)")
     ap.add_argument("--workload", choices=["chain", "kv", "sweep", "moe"], default="chain",
-                    help="chain: the driver's line (config 2); kv: LP->HP promotion (config 5); "
-                         "sweep: per-op token sweep (config 3); moe: routing (config 4)")
+                    help="chain: the headline op chain (the driver's line); kv: LP->HP "
+                         "promotion; sweep: per-op token sweep; moe: Mixtral-8x7B routing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     KV_NB = args.kv_blocks

@@ -124,7 +124,7 @@ def main():
         row["speedup"] = round(row["reference_cuda"]["us_per_launch"] / row["ours"]["us_per_launch"], 2)
         per_op[name] = row
     res["per_op"] = per_op
-    # MoE routing (config 4): the reference wrapper pre-fills sorted_ids with
+    # MoE routing (Mixtral-8x7B shapes): the reference wrapper pre-fills sorted_ids with
     # torch (fused_moe.py:191-195) before its moe_align_block_size; ours fills
     # the padding in the kernel.
     moe_r = load_ref_ops("moe_ops")

@@ -1,6 +1,6 @@
 """Restatement of the reference's KV move (KVhelper, paceserve/kv_transfer/kv_utils.py:33-56).
 
-TEST / BASELINE INFRASTRUCTURE ONLY: used by the tests as a layout oracle and
+TEST / MEASUREMENT INFRASTRUCTURE ONLY: used by the tests as a layout oracle and
 by bench.py's baseline leg to time the reference mechanism on the GPU box.
 PaceServe moves a sequence's blocks GPU -> CPU with one fancy-index gather
 per layer into a CPU tensor (kv_utils.py:44-46), ships it through the Ray

@@ -102,7 +102,7 @@ def test_kv_copy_through_c_abi():
 
 
 def test_promotion_sized_copy_single_gpu():
-    """BASELINE config-5 shapes (32 layers, 64 KiB slabs), 600 blocks, one GPU."""
+    """Promotion-workload shapes (32 layers, 64 KiB slabs), 600 blocks, one GPU."""
     L, nb, n = 32, 1024, 600
     src = make_cache(L, nb, seed=15)
     dst = [torch.zeros_like(s) for s in src]
