@@ -22,6 +22,9 @@ int cuda_fail(cudaError_t err, const char* what);
 bool pdl_enabled();
 // Number of SMs of `device`, cached.
 int sm_count(int device);
+// cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes) on `device`,
+// done once per (function, device) and size: repeated launches skip the call.
+cudaError_t ensure_dynamic_smem(const void* func, int device, int bytes);
 
 // The device the entry point launches on: the calling thread's current
 // device, which must own the stream (as for any CUDA launch).  No query is

@@ -339,7 +339,7 @@ int run_copy(void* const* src_layers, void* const* dst_layers, const void* src_f
     const int64_t grid = units < 2 * sms ? units : 2 * sms;
     const size_t smem = (size_t)kBulkStages * kBulkChunk;
     auto kern = kv_copy_bulk_kernel<MODE>;
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    err = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), guard.device(), (int)smem);
     if (err != cudaSuccess) return cuda_fail(err, what);
     err = launch(kern, dim3((unsigned)grid), dim3(32), smem, stream, st, dt,
                  static_cast<const char*>(src_flat), static_cast<char*>(dst_flat), src_ids,

@@ -676,7 +676,8 @@ extern "C" int pace_moe_align_block_size(const void* topk_ids, int ids_dtype, in
         auto kern = moe_align_cluster_kernel<I>;
         cudaError_t e = cudaSuccess;
         if (csmem > 48 * 1024)
-          e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
+          e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), guard.device(),
+                                  (int)csmem);
         if (e != cudaSuccess) return cuda_fail(e, "moe_align_block_size: cluster attributes");
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(g);
@@ -733,7 +734,7 @@ extern "C" int pace_moe_align_block_size(const void* topk_ids, int ids_dtype, in
     auto kern = staged ? moe_align_kernel<I, true> : moe_align_kernel<I, false>;
     if (smem > 48 * 1024) {
       cudaError_t e =
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+          ensure_dynamic_smem(reinterpret_cast<const void*>(kern), guard.device(), (int)smem);
       if (e != cudaSuccess) return cuda_fail(e, "moe_align_block_size: smem attribute");
     }
     cudaError_t err = launch(kern, dim3(1), dim3(nw * 32), (size_t)smem, stream,

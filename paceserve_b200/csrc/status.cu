@@ -6,6 +6,8 @@
 #include <atomic>
 #include <mutex>
 #include <string>
+#include <tuple>
+#include <vector>
 
 #include "common.cuh"
 
@@ -40,6 +42,19 @@ bool pdl_enabled() {
     g_pdl.store(v, std::memory_order_relaxed);
   }
   return v != 0;
+}
+
+cudaError_t ensure_dynamic_smem(const void* func, int device, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, int>> done;  // (func, device, bytes set)
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : done)
+    if (std::get<0>(e) == func && std::get<1>(e) == device && std::get<2>(e) >= bytes)
+      return cudaSuccess;
+  const cudaError_t err =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) done.emplace_back(func, device, bytes);
+  return err;
 }
 
 int sm_count(int device) {
