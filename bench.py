@@ -477,6 +477,35 @@ def _time_copy(fn, steps, warmup):
     return e0.elapsed_time(e1) / steps
 
 
+def kv_cpu_copy(src, dst, layers: int = 2):
+    """The block move done on the host cores: per layer, torch's fancy-index copy
+    dst[dst_ids] = src[src_ids] between host caches of the same shape, all
+    threads; a bounded sample of `layers` layers, scaled to GB/s."""
+    import torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(3)
+    # 2-byte elements as int16: the move is a byte copy, and integer equality
+    # has no NaN patterns
+    sc = [torch.randint(-30000, 30000, (KV_NB, *KV_SLAB), generator=g, dtype=torch.int16)
+          for _ in range(layers)]
+    dc = [torch.zeros(KV_NB, *KV_SLAB, dtype=torch.int16) for _ in range(layers)]
+    s_ids = torch.as_tensor(src, dtype=torch.long)
+    d_ids = torch.as_tensor(dst, dtype=torch.long)
+    dc[0][d_ids] = sc[0][s_ids]  # warm-up (first touch of the pages)
+    t0 = time.perf_counter()
+    for s_, d_ in zip(sc, dc):
+        d_[d_ids] = s_[s_ids]
+    dt = time.perf_counter() - t0
+    nbytes = layers * len(src) * KV_BLOCK_BYTES
+    ok = all(torch.equal(d_[d_ids], s_[s_ids]) for s_, d_ in zip(sc, dc))
+    return {"value": round(nbytes / dt / 1e9, 2), "unit": "GB/s", "cores": cores, "kind": "port",
+            "byte_exact": bool(ok),
+            "sample": f"{layers} of {KV_L} layers' block moves ({nbytes / 1e6:.0f} MB) as a host "
+                      f"fancy-index copy with {cores} threads"}
+
+
 def kv_reference_path(src_caches, dst_caches, src, dst, dev):
     """The reference mechanism (KVhelper GPU->CPU gather, CPU->GPU index-put), one pass."""
     import torch
@@ -616,6 +645,7 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True, overlap=False):
                                      "kind": "port", "sample": "KVhelper get_kv_cache/insert_kv_cache "
                                      "restated (per-layer fancy-index gather to host, index-put back), "
                                      "one pass, without the Ray object-store hop"}
+            out["cpu_baseline"] = kv_cpu_copy(src, dst)
         return out
 
     import torch.distributed as dist
