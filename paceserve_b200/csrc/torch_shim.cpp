@@ -52,6 +52,17 @@ void check_same_device(const Tensor& a, const Tensor& b, const char* op) {
               b.device(), ")");
 }
 
+// Device pointer of an optional int32 counter the kernel adds to, or null.  It
+// must live on the launching device: a host pointer would reach the kernel.
+int32_t* counter_ptr(const c10::optional<Tensor>& t, const at::Device& dev, const char* op,
+                     const char* name) {
+  if (!t.has_value()) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->device() == dev && t->scalar_type() == at::kInt &&
+                  t->numel() >= 1,
+              op, ": ", name, " must be an int32 tensor with at least one element on ", dev);
+  return t->data_ptr<int32_t>();
+}
+
 bool is_float_type(const Tensor& t) {
   return t.scalar_type() == at::kFloat || t.scalar_type() == at::kHalf ||
          t.scalar_type() == at::kBFloat16;
@@ -309,13 +320,7 @@ void run_kv_copy(const std::vector<void*>& src, const std::vector<void*>& dst,
   Tensor s = ids_on(src_ids, exec, op, "src_block_ids");
   Tensor d = ids_on(dst_ids, exec, op, "dst_block_ids");
   TORCH_CHECK(s.numel() == d.numel(), op, ": block id lists differ in length");
-  int32_t* bad = nullptr;
-  if (bad_pairs.has_value()) {
-    TORCH_CHECK(bad_pairs->scalar_type() == at::kInt && bad_pairs->device() == exec &&
-                    bad_pairs->numel() >= 1,
-                op, ": bad_pairs must be an int32 tensor on the executing device");
-    bad = bad_pairs->data_ptr<int32_t>();
-  }
+  int32_t* bad = counter_ptr(bad_pairs, exec, op, "bad_pairs");
   check_status(pace_kv_copy_blocks(src.data(), dst.data(), (int)src.size(),
                                    s.data_ptr<int32_t>(), d.data_ptr<int32_t>(), s.numel(),
                                    block_bytes, src_blocks, dst_blocks, bad, (int)method,
@@ -383,7 +388,7 @@ void gather_blocks(const std::vector<Tensor>& caches, const Tensor& block_ids, T
   TORCH_CHECK((int64_t)out.numel() * out.element_size() ==
                   (int64_t)c.ptrs.size() * ids.numel() * c.block_bytes,
               op, ": out must hold num_layers * len(block_ids) blocks");
-  int32_t* bad = bad_ids.has_value() ? bad_ids->data_ptr<int32_t>() : nullptr;
+  int32_t* bad = counter_ptr(bad_ids, c.device, op, "bad_ids");
   cudaStream_t st = at::cuda::getCurrentCUDAStream(c.device.index()).stream();
   check_status(pace_kv_gather_blocks(c.ptrs.data(), (int)c.ptrs.size(), ids.data_ptr<int32_t>(),
                                      ids.numel(), c.block_bytes, c.num_blocks, out.data_ptr(), bad,
@@ -404,7 +409,7 @@ void scatter_blocks(const Tensor& src, const std::vector<Tensor>& caches, const 
   TORCH_CHECK((int64_t)src.numel() * src.element_size() ==
                   (int64_t)c.ptrs.size() * ids.numel() * c.block_bytes,
               op, ": src must hold num_layers * len(block_ids) blocks");
-  int32_t* bad = bad_ids.has_value() ? bad_ids->data_ptr<int32_t>() : nullptr;
+  int32_t* bad = counter_ptr(bad_ids, c.device, op, "bad_ids");
   cudaStream_t st = at::cuda::getCurrentCUDAStream(c.device.index()).stream();
   check_status(pace_kv_scatter_blocks(src.data_ptr(), c.ptrs.data(), (int)c.ptrs.size(),
                                       ids.data_ptr<int32_t>(), ids.numel(), c.block_bytes,
@@ -475,7 +480,7 @@ void append_paged_kv_cache(const Tensor& append_key, const Tensor& append_value,
               ": batch_indices and positions need one entry per token");
   TORCH_CHECK(kp.numel() >= 1 && kl.numel() >= kp.numel() - 1, op,
               ": kv_indptr needs batch + 1 entries and kv_last_page_len batch entries");
-  int32_t* bad = bad_tokens.has_value() ? bad_tokens->data_ptr<int32_t>() : nullptr;
+  int32_t* bad = counter_ptr(bad_tokens, paged_kv_cache.device(), op, "bad_tokens");
   const at::cuda::CUDAGuard guard(paged_kv_cache.device());
   check_status(pace_append_paged_kv_cache(
                    append_key.data_ptr(), append_value.data_ptr(), nnz, (int)pc.heads, (int)pc.hd,
@@ -509,7 +514,7 @@ void append_paged_kv_cache_by_indptr(const Tensor& append_key, const Tensor& app
   Tensor kl = int32_on(kv_last_page_len, paged_kv_cache, op, "kv_last_page_len");
   TORCH_CHECK(ai.numel() == kp.numel() && kl.numel() >= kp.numel() - 1 && kp.numel() >= 1, op,
               ": append_indptr and kv_indptr need batch + 1 entries, kv_last_page_len batch");
-  int32_t* bad = bad_tokens.has_value() ? bad_tokens->data_ptr<int32_t>() : nullptr;
+  int32_t* bad = counter_ptr(bad_tokens, paged_kv_cache.device(), op, "bad_tokens");
   const at::cuda::CUDAGuard guard(paged_kv_cache.device());
   check_status(pace_append_paged_kv_cache_by_indptr(
                    append_key.data_ptr(), append_value.data_ptr(), nnz, (int)pc.heads,

@@ -101,6 +101,15 @@ def test_append_bad_tokens_skipped_and_counted():
     assert int(cache.ne(0).sum()) == 2 * nkv * hd
     with pytest.raises(RuntimeError, match="NHD"):
         kv.append_paged_kv_cache(key, value, bi, pos, cache, ki, kp, kl, "HND")
+    # a counter in host memory is rejected before any launch
+    with pytest.raises(RuntimeError, match="bad_tokens must be an int32 tensor"):
+        kv.append_paged_kv_cache(key, value, bi, pos, cache, ki, kp, kl, "NHD",
+                                 torch.zeros(1, dtype=torch.int32))
+    with pytest.raises(RuntimeError, match="bad_tokens must be an int32 tensor"):
+        kv.append_paged_kv_cache_by_indptr(key, value, torch.tensor([0, 4], dtype=torch.int32,
+                                                                    device=DEV),
+                                           cache, ki, kp, kl, torch.zeros(1, dtype=torch.int64,
+                                                                          device=DEV))
 
 
 def test_append_through_c_abi():
