@@ -158,11 +158,17 @@ int pace_moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel
  * The kernel runs on the current device (the stream's): the destination's device pulls over
  * NVLink, the source's device pushes.  Pairs with an id outside
  * [0, src_num_blocks) / [0, dst_num_blocks) are skipped and counted into
- * *bad_pairs (device int32, may be NULL; the caller zeroes it).  Destination
- * slabs must not overlap source slabs.  method: 0 = automatic, 1 = SIMT
- * 16-byte vector copy, 2 = bulk-async (TMA engine) copy staged through shared
- * memory.  block_bytes must be a multiple of 16 and every layer pointer
- * 16-byte aligned.
+ * *bad_pairs (device int32; the caller zeroes it).  Destination slabs must not
+ * overlap source slabs.  method: 0 = automatic, 1 = SIMT 16-byte vector copy,
+ * 2 = bulk-async (TMA engine) copy staged through shared memory.  bad_pairs
+ * may be NULL for methods 0 and 1; method 2 requires it, because its bounded
+ * waits report a timeout only there: PACE_KV_TIMEOUT_FLAG is OR-ed into
+ * *bad_pairs when a wait expired (that CTA stops copying, so the copy is
+ * incomplete), and PACE_KV_DRAIN_TIMEOUT_FLAG as well when a load was still
+ * in flight after a second wait -- it may then land in shared memory after
+ * the kernel exits, and the device must not be trusted further.  The return
+ * value only reports the launch.  block_bytes must be a multiple of 16 and
+ * every layer pointer 16-byte aligned.
  * Replaces the GPU->CPU->GPU move of KVhelper.get_kv_cache/insert_kv_cache
  * (paceserve/kv_transfer/kv_utils.py:33-56) used by BaseWorker._get_kv_cache/
  * _insert_kv_cache (paceserve/worker/base_worker.py:236-281). */
@@ -171,6 +177,50 @@ int pace_kv_copy_blocks(void* const* src_layers, void* const* dst_layers, int nu
                         int64_t num_pairs, int64_t block_bytes, int64_t src_num_blocks,
                         int64_t dst_num_blocks, int32_t* bad_pairs, int method,
                         cudaStream_t stream);
+
+/* Flags OR-ed into *bad_pairs by the bulk method (see pace_kv_copy_blocks). */
+#define PACE_KV_TIMEOUT_FLAG (1 << 30)
+#define PACE_KV_DRAIN_TIMEOUT_FLAG (1 << 29)
+
+/* Options of pace_kv_copy_blocks_ex.  Zero-initialise, then set fields. */
+typedef struct pace_kv_copy_opts {
+  int method;             /* as pace_kv_copy_blocks */
+  int max_ctas;           /* > 0: at most this many CTAs (a budget of SMs left to
+                             other work on the device); 0: no cap */
+  uint64_t wait_limit_ns; /* bulk method: bound of every wait; 0 = 2 s */
+  int test_overarm_bytes; /* TESTS ONLY, must be 0 otherwise: with method 2, the
+                             first load of CTA 0 tells its barrier to expect this
+                             many bytes (a multiple of 16) more than it copies, so
+                             that wait expires -- how the timeout path is tested
+                             without a GPU fault */
+} pace_kv_copy_opts;
+
+/* pace_kv_copy_blocks with options: a CTA budget and the bulk method's wait
+ * bound.  New: no reference counterpart (the reference moves KV through the
+ * host, paceserve/kv_transfer/kv_utils.py:33-56). */
+int pace_kv_copy_blocks_ex(void* const* src_layers, void* const* dst_layers, int num_layers,
+                           const int32_t* src_block_ids, const int32_t* dst_block_ids,
+                           int64_t num_pairs, int64_t block_bytes, int64_t src_num_blocks,
+                           int64_t dst_num_blocks, int32_t* bad_pairs,
+                           const pace_kv_copy_opts* opts, cudaStream_t stream);
+
+/* The same block copy on the copy engines: no kernel, no SM.  Block ids are
+ * HOST int32 arrays (the block manager's tables).  Pairs are ordered by source
+ * id; each run of pairs whose source and destination ids are both consecutive
+ * becomes one cudaMemcpyAsync per layer, or one cudaMemcpy2DAsync covering all
+ * layers when both layer tables are evenly spaced.  Invalid pairs are skipped
+ * and their number stored in *bad_pairs (host, may be NULL); *copies_issued
+ * (host, may be NULL) receives the number of copies queued on `stream`.  The
+ * host cost grows with the number of runs, so fragmented block tables make
+ * this path slower to issue than the kernel.  Duplicate destination ids leave
+ * that block with one of their sources, unspecified which.
+ * Replaces, like pace_kv_copy_blocks, the host round trip of
+ * paceserve/kv_transfer/kv_utils.py:33-56. */
+int pace_kv_copy_blocks_ce(void* const* src_layers, void* const* dst_layers, int num_layers,
+                           const int32_t* src_block_ids, const int32_t* dst_block_ids,
+                           int64_t num_pairs, int64_t block_bytes, int64_t src_num_blocks,
+                           int64_t dst_num_blocks, int64_t* bad_pairs, int64_t* copies_issued,
+                           cudaStream_t stream);
 
 /* Gather blocks block_ids[0..n) of every layer into out, laid out
  * [num_layers, n, block_bytes] contiguous.  out may be device memory or

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_uint64, c_void_p
 
 LIBRARY_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libpace_b200.so")
 
@@ -22,6 +22,16 @@ PACE_ERR_TOO_LARGE = 5
 PACE_F32, PACE_F16, PACE_BF16 = 0, 1, 2
 PACE_U8, PACE_I8, PACE_I16, PACE_I32, PACE_I64 = 3, 4, 5, 6, 7
 PACE_IPC_HANDLE_BYTES = 64
+PACE_KV_TIMEOUT_FLAG = 1 << 30
+PACE_KV_DRAIN_TIMEOUT_FLAG = 1 << 29
+
+
+class KvCopyOpts(ctypes.Structure):
+    """``pace_kv_copy_opts``."""
+
+    _fields_ = [("method", c_int), ("max_ctas", c_int), ("wait_limit_ns", c_uint64),
+                ("test_overarm_bytes", c_int)]
+
 
 _P = c_void_p  # device pointer / stream
 _ACT = [_P, _P, c_int64, c_int64, c_int64, c_int64, c_int, _P]
@@ -57,6 +67,16 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [POINTER(c_void_p), POINTER(c_void_p), c_int, _P, _P, c_int64, c_int64, c_int64, c_int64,
          _P, c_int, _P],
+    ),
+    "pace_kv_copy_blocks_ex": (
+        c_int,
+        [POINTER(c_void_p), POINTER(c_void_p), c_int, _P, _P, c_int64, c_int64, c_int64, c_int64,
+         _P, POINTER(KvCopyOpts), _P],
+    ),
+    "pace_kv_copy_blocks_ce": (
+        c_int,
+        [POINTER(c_void_p), POINTER(c_void_p), c_int, POINTER(c_int32), POINTER(c_int32), c_int64,
+         c_int64, c_int64, c_int64, POINTER(c_int64), POINTER(c_int64), _P],
     ),
     "pace_kv_gather_blocks": (
         c_int,

@@ -114,6 +114,13 @@ __device__ __forceinline__ uint4 ld_v4(const void* p) {
                : "memory");
   return v;
 }
+// 8-byte load cached at L2 only: a second read of a location sees what L2
+// holds now, never a stale L1 line from a read earlier in the same kernel.
+__device__ __forceinline__ int64_t ld_cg_s64(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_v4(void* p, const uint4& v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)

@@ -42,7 +42,9 @@ struct AppendJob {
 
 // Page and slot of a token of request b at sequence position pos, or false
 // if any index is out of range.  ip / last: kv_indptr and kv_last_page_len
-// (global or staged copies).
+// (global or staged copies).  A last-page length outside [1, page_size] makes
+// the request's length inconsistent with its page count, so its tokens are
+// rejected rather than placed on a page past the request's range.
 __device__ __forceinline__ bool locate_token(const AppendJob& j, int b, int64_t pos,
                                              const int32_t* kv_indices, const int32_t* ip,
                                              const int32_t* last, int64_t* page, int* slot) {
@@ -50,8 +52,10 @@ __device__ __forceinline__ bool locate_token(const AppendJob& j, int b, int64_t 
   const int64_t p0 = ip[b];
   const int64_t np = (int64_t)ip[b + 1] - p0;
   if (np <= 0 || p0 < 0 || p0 + np > j.num_indices) return false;
-  const int64_t seq_len = (np - 1) * j.page_size + last[b];
-  if (pos >= seq_len) return false;
+  const int64_t lp = last[b];
+  if (lp < 1 || lp > j.page_size) return false;
+  const int64_t seq_len = (np - 1) * j.page_size + lp;
+  if (pos >= seq_len) return false;  // so pos / page_size < np
   const int64_t pg = kv_indices[p0 + pos / j.page_size];
   if (pg < 0 || pg >= j.num_pages) return false;
   *page = pg;
@@ -132,9 +136,15 @@ __global__ void __launch_bounds__(kAppendThreads)
     if (BY_INDPTR) {
       const int32_t* ai = STAGED ? s_ai : append_indptr;
       b = find_request(ai, job.batch, i);
-      const int64_t np = (int64_t)ip[b + 1] - ip[b];
-      const int64_t seq_len = (np - 1) * job.page_size + last[b];
-      pos = seq_len - ((int64_t)ai[b + 1] - ai[b]) + (i - ai[b]);
+      if (i < (int64_t)ai[b] || i >= (int64_t)ai[b + 1]) {
+        // append_indptr does not cover token i (it does not start at 0, or is
+        // not ascending): no request owns the token.
+        b = -1;
+      } else {
+        const int64_t np = (int64_t)ip[b + 1] - ip[b];
+        const int64_t seq_len = (np - 1) * job.page_size + last[b];
+        pos = seq_len - ((int64_t)ai[b + 1] - ai[b]) + (i - ai[b]);
+      }
     }
     int64_t page;
     int slot;

@@ -26,6 +26,9 @@
 // counted, never dereferenced.
 #include <cuda.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "common.cuh"
 
 namespace pace {
@@ -37,8 +40,9 @@ constexpr int kUnroll = 8;                              // 16-byte vectors per t
 constexpr int64_t kChunk = kThreads * kUnroll * 16;     // 32 KiB per SIMT unit
 constexpr int kBulkStages = 6;
 constexpr int64_t kBulkChunk = 16 * 1024;               // bytes per bulk stage
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
-constexpr int32_t kTimeoutFlag = 1 << 30;
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;  // 2 s
+constexpr int32_t kTimeoutFlag = PACE_KV_TIMEOUT_FLAG;
+constexpr int32_t kDrainTimeoutFlag = PACE_KV_DRAIN_TIMEOUT_FLAG;
 
 struct LayerTable {
   char* p[kMaxLayers];
@@ -52,6 +56,8 @@ struct Job {
   int64_t block_bytes;
   int64_t src_blocks;  // bound for src ids (paged source)
   int64_t dst_blocks;  // bound for dst ids (paged destination)
+  unsigned long long wait_limit_ns;  // bulk path: bound of every mbarrier wait
+  uint32_t overarm_bytes;            // bulk path, tests only (pace_kv_copy_opts)
 };
 
 // Source/destination address of (layer l, pair j), or nullptr if the pair's
@@ -143,18 +149,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait; false when the limit expired.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait; false when `limit_ns` expired.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
   return true;
 }
+// expect_bytes is `bytes` except in the over-arm test, where the barrier is
+// told to expect more than the copy delivers, so its phase never completes.
 __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes,
-                                          uint32_t bar) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                                          uint32_t bar, uint32_t expect_bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(expect_bytes)
                : "memory");
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -224,7 +234,8 @@ __global__ void __launch_bounds__(32)
     st_dst[s] = dp + off;
     st_bytes[s] = bytes;
     pending[s] = true;
-    bulk_load(smem_addr(stage_mem + s * kBulkChunk), sp + off, bytes, smem_addr(&bars[s]));
+    const uint32_t expect = (i == 0 && blockIdx.x == 0) ? bytes + job.overarm_bytes : bytes;
+    bulk_load(smem_addr(stage_mem + s * kBulkChunk), sp + off, bytes, smem_addr(&bars[s]), expect);
   };
 
   const int64_t pro = my_units < kBulkStages ? my_units : kBulkStages;
@@ -232,7 +243,7 @@ __global__ void __launch_bounds__(32)
   for (int64_t i = 0; i < my_units; ++i) {
     const int s = (int)(i % kBulkStages);
     if (pending[s]) {
-      if (!mbar_wait(smem_addr(&bars[s]), uses[s] & 1u)) {
+      if (!mbar_wait(smem_addr(&bars[s]), uses[s] & 1u, job.wait_limit_ns)) {
         timed_out = true;
         break;
       }
@@ -250,10 +261,16 @@ __global__ void __launch_bounds__(32)
     }
   }
   if (timed_out) {
-    if (bad) atomicOr(bad, kTimeoutFlag);
-    // Drain loads still in flight (bounded), so no copy lands after exit.
+    // No new load is issued after a timeout.  Every load still in flight is
+    // waited for once more (same bound) so that none lands in this CTA's shared
+    // memory after it exits.  A load that outlasts that second bound too (a
+    // source that stopped answering) cannot be cancelled: the drain flag tells
+    // the caller the device may hold a late write and must not be trusted.
+    int32_t flags = kTimeoutFlag;
     for (int s = 0; s < kBulkStages; ++s)
-      if (pending[s]) mbar_wait(smem_addr(&bars[s]), uses[s] & 1u);
+      if (pending[s] && !mbar_wait(smem_addr(&bars[s]), uses[s] & 1u, job.wait_limit_ns))
+        flags |= kDrainTimeoutFlag;
+    atomicOr(bad, flags);
   }
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
@@ -290,11 +307,19 @@ int check_layers(void* const* layers, int num_layers, const char* what) {
   return PACE_OK;
 }
 
+struct CopyOpts {
+  int method = 0;          // 0 auto, 1 SIMT, 2 bulk
+  int max_ctas = 0;        // 0: no cap
+  unsigned long long wait_limit_ns = kDefaultWaitLimitNs;
+  uint32_t overarm_bytes = 0;
+};
+
 template <int MODE>
 int run_copy(void* const* src_layers, void* const* dst_layers, const void* src_flat, void* dst_flat,
              int num_layers, const int32_t* src_ids, const int32_t* dst_ids, int64_t n,
-             int64_t block_bytes, int64_t src_blocks, int64_t dst_blocks, int32_t* bad, int method,
-             cudaStream_t stream, const char* what) {
+             int64_t block_bytes, int64_t src_blocks, int64_t dst_blocks, int32_t* bad,
+             const CopyOpts& opt, cudaStream_t stream, const char* what) {
+  const int method = opt.method;
   if (num_layers <= 0 || num_layers > kMaxLayers)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: num_layers %d outside [1, %d]", what, num_layers,
                 kMaxLayers);
@@ -320,7 +345,14 @@ int run_copy(void* const* src_layers, void* const* dst_layers, const void* src_f
   } else if (!dst_flat || !aligned16(dst_flat)) {
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: destination buffer null or unaligned", what);
   }
-  Job job{num_layers, n, block_bytes, src_blocks, dst_blocks};
+  if (method == 2 && !bad)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: the bulk method reports wait timeouts only through bad_pairs, which must "
+                "not be NULL", what);
+  if (opt.max_ctas < 0 || opt.overarm_bytes % 16 != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad copy options", what);
+  Job job{num_layers, n,  block_bytes, src_blocks, dst_blocks, opt.wait_limit_ns,
+          opt.overarm_bytes};
   StreamDeviceGuard guard(stream);
   if (MODE == kContigToPaged) {
     int rc = device_view(src_flat, &src_flat, what);
@@ -336,7 +368,8 @@ int run_copy(void* const* src_layers, void* const* dst_layers, const void* src_f
   cudaError_t err;
   if (method == 2) {
     const int64_t units = (int64_t)num_layers * n * ceil_div(block_bytes, kBulkChunk);
-    const int64_t grid = units < 2 * sms ? units : 2 * sms;
+    int64_t grid = units < 2 * sms ? units : 2 * sms;
+    if (opt.max_ctas > 0 && grid > opt.max_ctas) grid = opt.max_ctas;
     const size_t smem = (size_t)kBulkStages * kBulkChunk;
     auto kern = kv_copy_bulk_kernel<MODE>;
     err = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), guard.device(), (int)smem);
@@ -350,7 +383,8 @@ int run_copy(void* const* src_layers, void* const* dst_layers, const void* src_f
     // copy peak in HBM traffic) against 2963 GB/s with one resident wave of
     // 8 CTAs per SM looping over the units.
     const int64_t units = (int64_t)num_layers * n * ceil_div(block_bytes, kChunk);
-    const int64_t grid = units < INT32_MAX ? units : INT32_MAX;
+    int64_t grid = units < INT32_MAX ? units : INT32_MAX;
+    if (opt.max_ctas > 0 && grid > opt.max_ctas) grid = opt.max_ctas;
     err = launch(kv_copy_simt_kernel<MODE>, dim3((unsigned)grid), dim3(kThreads), 0, stream, st,
                  dt, static_cast<const char*>(src_flat), static_cast<char*>(dst_flat), src_ids,
                  dst_ids, job, bad);
@@ -368,12 +402,36 @@ extern "C" int pace_kv_copy_blocks(void* const* src_layers, void* const* dst_lay
                                    int64_t block_bytes, int64_t src_num_blocks,
                                    int64_t dst_num_blocks, int32_t* bad_pairs, int method,
                                    cudaStream_t stream) {
+  pace_kv_copy_opts opts = {};
+  opts.method = method;
+  return pace_kv_copy_blocks_ex(src_layers, dst_layers, num_layers, src_block_ids, dst_block_ids,
+                                num_pairs, block_bytes, src_num_blocks, dst_num_blocks, bad_pairs,
+                                &opts, stream);
+}
+
+extern "C" int pace_kv_copy_blocks_ex(void* const* src_layers, void* const* dst_layers,
+                                      int num_layers, const int32_t* src_block_ids,
+                                      const int32_t* dst_block_ids, int64_t num_pairs,
+                                      int64_t block_bytes, int64_t src_num_blocks,
+                                      int64_t dst_num_blocks, int32_t* bad_pairs,
+                                      const pace_kv_copy_opts* opts, cudaStream_t stream) {
   using namespace pace;
-  if (method < 0 || method > 2)
-    return fail(PACE_ERR_INVALID_ARGUMENT, "kv_copy_blocks: method %d not in {0,1,2}", method);
+  if (!opts) return fail(PACE_ERR_INVALID_ARGUMENT, "kv_copy_blocks: null options");
+  if (opts->method < 0 || opts->method > 2)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "kv_copy_blocks: method %d not in {0,1,2}",
+                opts->method);
+  CopyOpts o;
+  o.method = opts->method;
+  o.max_ctas = opts->max_ctas;
+  o.wait_limit_ns = opts->wait_limit_ns ? opts->wait_limit_ns : kDefaultWaitLimitNs;
+  if (opts->test_overarm_bytes < 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "kv_copy_blocks: negative test_overarm_bytes");
+  o.overarm_bytes = (uint32_t)opts->test_overarm_bytes;
+  if (o.overarm_bytes && o.method != 2)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "kv_copy_blocks: test_overarm_bytes needs method 2");
   return run_copy<kPagedToPaged>(src_layers, dst_layers, nullptr, nullptr, num_layers,
                                  src_block_ids, dst_block_ids, num_pairs, block_bytes,
-                                 src_num_blocks, dst_num_blocks, bad_pairs, method, stream,
+                                 src_num_blocks, dst_num_blocks, bad_pairs, o, stream,
                                  "kv_copy_blocks");
 }
 
@@ -381,8 +439,10 @@ extern "C" int pace_kv_gather_blocks(void* const* layers, int num_layers, const 
                                      int64_t n, int64_t block_bytes, int64_t num_blocks, void* out,
                                      int32_t* bad_ids, cudaStream_t stream) {
   using namespace pace;
+  CopyOpts o;
+  o.method = 1;
   return run_copy<kPagedToContig>(layers, nullptr, nullptr, out, num_layers, block_ids, nullptr, n,
-                                  block_bytes, num_blocks, 0, bad_ids, 1, stream,
+                                  block_bytes, num_blocks, 0, bad_ids, o, stream,
                                   "kv_gather_blocks");
 }
 
@@ -390,9 +450,110 @@ extern "C" int pace_kv_scatter_blocks(const void* in, void* const* layers, int n
                                       const int32_t* block_ids, int64_t n, int64_t block_bytes,
                                       int64_t num_blocks, int32_t* bad_ids, cudaStream_t stream) {
   using namespace pace;
+  CopyOpts o;
+  o.method = 1;
   return run_copy<kContigToPaged>(nullptr, layers, in, nullptr, num_layers, nullptr, block_ids, n,
-                                  block_bytes, 0, num_blocks, bad_ids, 1, stream,
+                                  block_bytes, 0, num_blocks, bad_ids, o, stream,
                                   "kv_scatter_blocks");
+}
+
+// ------------------------------------------------- copy-engine path ------
+// Block copy with the GPU's copy engines instead of its SMs: one
+// cudaMemcpyAsync per run of pairs whose source and destination ids are both
+// consecutive, per layer -- or one cudaMemcpy2DAsync per run covering every
+// layer when both layer tables are evenly spaced (one allocation viewed per
+// layer).  No kernel runs, so a promotion this way leaves every SM to the
+// serving instance.  The ids are host arrays (the block manager's tables);
+// pairs are ordered by source id before the runs are formed.
+namespace pace {
+namespace {
+
+struct Pair {
+  int64_t s, d;
+};
+
+// Byte distance between consecutive layer pointers when it is the same for all
+// layers and positive, else 0.
+int64_t uniform_stride(void* const* layers, int num_layers) {
+  if (num_layers < 2) return 0;
+  const int64_t st = reinterpret_cast<const char*>(layers[1]) - reinterpret_cast<const char*>(layers[0]);
+  if (st <= 0) return 0;
+  for (int l = 2; l < num_layers; ++l)
+    if (reinterpret_cast<const char*>(layers[l]) - reinterpret_cast<const char*>(layers[l - 1]) != st)
+      return 0;
+  return st;
+}
+
+}  // namespace
+}  // namespace pace
+
+extern "C" int pace_kv_copy_blocks_ce(void* const* src_layers, void* const* dst_layers,
+                                      int num_layers, const int32_t* src_block_ids,
+                                      const int32_t* dst_block_ids, int64_t num_pairs,
+                                      int64_t block_bytes, int64_t src_num_blocks,
+                                      int64_t dst_num_blocks, int64_t* bad_pairs,
+                                      int64_t* copies_issued, cudaStream_t stream) {
+  using namespace pace;
+  const char* what = "kv_copy_blocks_ce";
+  if (num_layers <= 0 || num_layers > kMaxLayers)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: num_layers %d outside [1, %d]", what, num_layers,
+                kMaxLayers);
+  if (num_pairs < 0 || block_bytes <= 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: need num_pairs >= 0 and block_bytes > 0", what);
+  if (bad_pairs) *bad_pairs = 0;
+  if (copies_issued) *copies_issued = 0;
+  if (num_pairs == 0) return PACE_OK;
+  if (!src_block_ids || !dst_block_ids)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null block id array", what);
+  int rc = check_layers(src_layers, num_layers, what);
+  if (rc) return rc;
+  rc = check_layers(dst_layers, num_layers, what);
+  if (rc) return rc;
+  std::vector<Pair> pairs;
+  pairs.reserve((size_t)num_pairs);
+  int64_t bad = 0;
+  for (int64_t j = 0; j < num_pairs; ++j) {
+    const int64_t sb = src_block_ids[j], db = dst_block_ids[j];
+    if (sb < 0 || sb >= src_num_blocks || db < 0 || db >= dst_num_blocks) {
+      ++bad;
+      continue;
+    }
+    pairs.push_back({sb, db});
+  }
+  if (bad_pairs) *bad_pairs = bad;
+  std::stable_sort(pairs.begin(), pairs.end(), [](const Pair& a, const Pair& b) { return a.s < b.s; });
+  const int64_t ss = uniform_stride(src_layers, num_layers);
+  const int64_t ds = uniform_stride(dst_layers, num_layers);
+  const bool two_d = ss >= block_bytes && ds >= block_bytes;
+  int64_t issued = 0;
+  size_t i = 0;
+  while (i < pairs.size()) {
+    size_t j = i + 1;
+    while (j < pairs.size() && pairs[j].s == pairs[j - 1].s + 1 && pairs[j].d == pairs[j - 1].d + 1)
+      ++j;
+    const size_t run = (size_t)(j - i) * (size_t)block_bytes;
+    const int64_t so = pairs[i].s * block_bytes, doff = pairs[i].d * block_bytes;
+    if (two_d && (size_t)ss >= run && (size_t)ds >= run) {
+      const cudaError_t err = cudaMemcpy2DAsync(
+          static_cast<char*>(dst_layers[0]) + doff, (size_t)ds,
+          static_cast<const char*>(src_layers[0]) + so, (size_t)ss, run, (size_t)num_layers,
+          cudaMemcpyDefault, stream);
+      if (err != cudaSuccess) return cuda_fail(err, what);
+      ++issued;
+    } else {
+      for (int l = 0; l < num_layers; ++l) {
+        const cudaError_t err =
+            cudaMemcpyAsync(static_cast<char*>(dst_layers[l]) + doff,
+                            static_cast<const char*>(src_layers[l]) + so, run, cudaMemcpyDefault,
+                            stream);
+        if (err != cudaSuccess) return cuda_fail(err, what);
+        ++issued;
+      }
+    }
+    i = j;
+  }
+  if (copies_issued) *copies_issued = issued;
+  return PACE_OK;
 }
 
 // ------------------------------------------------------ peer access / IPC --

@@ -199,6 +199,89 @@ __global__ void __launch_bounds__(kMaxThreads)
   }
 }
 
+// Exact-fit vector path for 16-bit rows: hidden == NT * NV * 8 at compile
+// time, so every thread owns exactly NV vectors (no per-vector guards), the
+// CTA size and warp count are constants, and the mean's divisor is a
+// constant (a power of two becomes an exact multiply).  WASM: the weight is
+// loaded with the same ordered vector load as the row, so it is in flight
+// together with the row instead of wherever the compiler schedules it.
+// Arithmetic, rounding points and reduction order per thread/warp are those
+// of rms_norm_vec_kernel.
+template <typename T, int NT, int NV, bool FUSED, bool WASM>
+__global__ void __launch_bounds__(NT)
+    rms_norm_exact_kernel(const T* x_in, T* x_out, T* res, const T* __restrict__ weight, float eps,
+                          int64_t in_stride, int64_t out_stride, int64_t res_stride) {
+  using Tr = Traits<T>;
+  constexpr int V = Tr::kVec;
+  constexpr int HID = NT * NV * V;
+  constexpr int NW = NT / 32;
+  static_assert(NT % 32 == 0 && NW <= 32, "");
+  __shared__ float red[NW];
+  const int64_t row = blockIdx.x;
+  const T* xr = x_in + row * in_stride;
+  T* orow = x_out + row * out_stride;
+  T* rr = FUSED ? res + row * res_stride : nullptr;
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    prefetch_l2(xr, HID * (int)sizeof(T));
+    if (FUSED) prefetch_l2(rr, HID * (int)sizeof(T));
+    if (row < 4) prefetch_l2(weight, HID * (int)sizeof(T));
+  }
+  pdl_wait();
+  uint4 a[NV], b[NV], wv[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = threadIdx.x + j * NT;
+    if (FUSED) {
+      a[j] = ld_v4(xr + c * V);
+      b[j] = ld_v4(rr + c * V);
+    } else {
+      a[j] = ld_nc_v4(xr + c * V);
+    }
+    wv[j] = WASM ? ld_nc_v4(weight + c * V) : __ldg(reinterpret_cast<const uint4*>(weight) + c);
+  }
+  float v[NV][V];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = threadIdx.x + j * NT;
+    Tr::unpack(a[j], v[j]);
+    if (FUSED) {
+      float q[V];
+      Tr::unpack(b[j], q);
+#pragma unroll
+      for (int e = 0; e < V; ++e) v[j][e] = Tr::round(v[j][e] + q[e]);
+      st_v4(rr + c * V, Tr::pack(v[j]));
+    }
+#pragma unroll
+    for (int e = 0; e < V; ++e) ss += v[j][e] * v[j][e];
+  }
+  ss = warp_sum(ss);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float total = ss;
+  if (NW > 1) {
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (NW > 8) {
+      total = warp_sum(lane < NW ? red[lane] : 0.f);
+    } else {
+      total = 0.f;
+#pragma unroll
+      for (int i = 0; i < NW; ++i) total += red[i];
+    }
+  }
+  const float inv = rsqrtf(total / (float)HID + eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = threadIdx.x + j * NT;
+    float w[V], o[V];
+    Tr::unpack(wv[j], w);
+#pragma unroll
+    for (int e = 0; e < V; ++e) o[e] = Tr::round(v[j][e] * inv) * w[e];
+    st_v4(orow + c * V, Tr::pack(o));
+  }
+}
+
 // Rows per CTA of the plain norm's vector path (1 = rms_norm_vec_kernel).
 // Measured on B200: two rows per CTA are 8-9 % faster (8B) and 3-4 % faster
 // (70B) at T >= 8192, 5 % slower at T = 2048 and 45 % slower at T = 512, where

@@ -303,28 +303,74 @@ CacheSet cache_set(const std::vector<Tensor>& caches, const char* op, const char
   return s;
 }
 
+// Block ids as a contiguous int32 tensor on `dev`.  int64 ids outside
+// [0, INT32_MAX] become -1 before narrowing (on the device, no synchronisation),
+// so the kernel skips and counts them instead of a wrapped id selecting a
+// valid block.
 Tensor ids_on(const Tensor& ids, const c10::Device& dev, const char* op, const char* name) {
   TORCH_CHECK(ids.dim() == 1, op, ": ", name, " must be 1-D");
   TORCH_CHECK(ids.scalar_type() == at::kInt || ids.scalar_type() == at::kLong, op, ": ", name,
               " must be int32 or int64");
+  if (ids.scalar_type() == at::kLong) {
+    Tensor t = ids.to(dev, /*non_blocking=*/false, /*copy=*/false);
+    t = at::where(t.lt(0).logical_or(t.gt((int64_t)INT32_MAX)), at::full_like(t, -1), t);
+    return t.to(at::kInt).contiguous();
+  }
   return ids.to(dev, at::kInt, /*non_blocking=*/false, /*copy=*/false).contiguous();
+}
+
+// Method 3 of the Python-facing copies: the copy engines (pace_kv_copy_blocks_ce).
+constexpr int64_t kMethodCopyEngine = 3;
+
+// Host int32 copy of a 1-D id tensor (a device tensor is copied to the host,
+// which synchronises with its stream).  int64 ids outside int32 become -1.
+std::vector<int32_t> host_ids(const Tensor& ids, const char* op, const char* name) {
+  TORCH_CHECK(ids.dim() == 1, op, ": ", name, " must be 1-D");
+  TORCH_CHECK(ids.scalar_type() == at::kInt || ids.scalar_type() == at::kLong, op, ": ", name,
+              " must be int32 or int64");
+  Tensor t = ids.to(at::kCPU).to(at::kLong).contiguous();
+  const int64_t* p = t.data_ptr<int64_t>();
+  std::vector<int32_t> out((size_t)t.numel());
+  for (int64_t i = 0; i < t.numel(); ++i)
+    out[(size_t)i] = (p[i] < 0 || p[i] > (int64_t)INT32_MAX) ? -1 : (int32_t)p[i];
+  return out;
 }
 
 void run_kv_copy(const std::vector<void*>& src, const std::vector<void*>& dst,
                  int64_t src_blocks, int64_t dst_blocks, int64_t block_bytes,
                  const c10::Device& exec, const Tensor& src_ids, const Tensor& dst_ids,
-                 int64_t method, const c10::optional<Tensor>& bad_pairs, const char* op) {
+                 int64_t method, const c10::optional<Tensor>& bad_pairs, int64_t max_ctas,
+                 int64_t wait_limit_ns, const char* op) {
   TORCH_CHECK(src.size() == dst.size(), op, ": source and destination layer counts differ (",
               src.size(), " vs ", dst.size(), ")");
   const at::cuda::CUDAGuard guard(exec);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(exec.index()).stream();
+  if (method == kMethodCopyEngine) {
+    std::vector<int32_t> s = host_ids(src_ids, op, "src_block_ids");
+    std::vector<int32_t> d = host_ids(dst_ids, op, "dst_block_ids");
+    TORCH_CHECK(s.size() == d.size(), op, ": block id lists differ in length");
+    counter_ptr(bad_pairs, exec, op, "bad_pairs");  // validates the counter before any copy
+    int64_t nbad = 0, issued = 0;
+    check_status(pace_kv_copy_blocks_ce(src.data(), dst.data(), (int)src.size(), s.data(),
+                                        d.data(), (int64_t)s.size(), block_bytes, src_blocks,
+                                        dst_blocks, &nbad, &issued, stream),
+                 op);
+    if (bad_pairs.has_value() && nbad > 0) bad_pairs->add_(nbad);  // stream-ordered, as the kernels count
+    return;
+  }
   Tensor s = ids_on(src_ids, exec, op, "src_block_ids");
   Tensor d = ids_on(dst_ids, exec, op, "dst_block_ids");
   TORCH_CHECK(s.numel() == d.numel(), op, ": block id lists differ in length");
   int32_t* bad = counter_ptr(bad_pairs, exec, op, "bad_pairs");
-  check_status(pace_kv_copy_blocks(src.data(), dst.data(), (int)src.size(),
-                                   s.data_ptr<int32_t>(), d.data_ptr<int32_t>(), s.numel(),
-                                   block_bytes, src_blocks, dst_blocks, bad, (int)method,
-                                   at::cuda::getCurrentCUDAStream(exec.index()).stream()),
+  TORCH_CHECK(method != 2 || bad != nullptr, op,
+              ": method 2 reports wait timeouts through bad_pairs; pass an int32 counter");
+  pace_kv_copy_opts opts = {};
+  opts.method = (int)method;
+  opts.max_ctas = (int)max_ctas;
+  opts.wait_limit_ns = (uint64_t)wait_limit_ns;
+  check_status(pace_kv_copy_blocks_ex(src.data(), dst.data(), (int)src.size(),
+                                      s.data_ptr<int32_t>(), d.data_ptr<int32_t>(), s.numel(),
+                                      block_bytes, src_blocks, dst_blocks, bad, &opts, stream),
                op);
   // Device copies of the ids were allocated on this same stream, so the
   // caching allocator cannot hand their memory out before the kernel ran.
@@ -334,7 +380,8 @@ void run_kv_copy(const std::vector<void*>& src, const std::vector<void*>& dst,
 // Runs on the destination device (pull) unless push=True.
 void copy_blocks_p2p(const std::vector<Tensor>& src_caches, const std::vector<Tensor>& dst_caches,
                      const Tensor& src_block_ids, const Tensor& dst_block_ids, int64_t method,
-                     bool push, const c10::optional<Tensor>& bad_pairs) {
+                     bool push, const c10::optional<Tensor>& bad_pairs, int64_t max_ctas,
+                     int64_t wait_limit_ns) {
   const char* op = "copy_blocks_p2p";
   CacheSet s = cache_set(src_caches, op, "src_caches");
   CacheSet d = cache_set(dst_caches, op, "dst_caches");
@@ -344,7 +391,7 @@ void copy_blocks_p2p(const std::vector<Tensor>& src_caches, const std::vector<Te
   if (exec != other)
     check_status(pace_enable_peer_access(exec.index(), other.index()), op);
   run_kv_copy(s.ptrs, d.ptrs, s.num_blocks, d.num_blocks, s.block_bytes, exec, src_block_ids,
-              dst_block_ids, method, bad_pairs, op);
+              dst_block_ids, method, bad_pairs, max_ctas, wait_limit_ns, op);
 }
 
 // Same, with the source given as raw per-layer pointers (e.g. mapped from
@@ -352,26 +399,28 @@ void copy_blocks_p2p(const std::vector<Tensor>& src_caches, const std::vector<Te
 void copy_blocks_from_ptrs(const std::vector<int64_t>& src_ptrs, int64_t src_num_blocks,
                            const std::vector<Tensor>& dst_caches, const Tensor& src_block_ids,
                            const Tensor& dst_block_ids, int64_t method,
-                           const c10::optional<Tensor>& bad_pairs) {
+                           const c10::optional<Tensor>& bad_pairs, int64_t max_ctas,
+                           int64_t wait_limit_ns) {
   const char* op = "copy_blocks_from_ptrs";
   CacheSet d = cache_set(dst_caches, op, "dst_caches");
   std::vector<void*> s;
   for (int64_t p : src_ptrs) s.push_back(reinterpret_cast<void*>(p));
   run_kv_copy(s, d.ptrs, src_num_blocks, d.num_blocks, d.block_bytes, d.device, src_block_ids,
-              dst_block_ids, method, bad_pairs, op);
+              dst_block_ids, method, bad_pairs, max_ctas, wait_limit_ns, op);
 }
 
 // Destination given as raw pointers (push into another process's cache).
 void copy_blocks_to_ptrs(const std::vector<Tensor>& src_caches, const std::vector<int64_t>& dst_ptrs,
                          int64_t dst_num_blocks, const Tensor& src_block_ids,
                          const Tensor& dst_block_ids, int64_t method,
-                         const c10::optional<Tensor>& bad_pairs) {
+                         const c10::optional<Tensor>& bad_pairs, int64_t max_ctas,
+                         int64_t wait_limit_ns) {
   const char* op = "copy_blocks_to_ptrs";
   CacheSet s = cache_set(src_caches, op, "src_caches");
   std::vector<void*> d;
   for (int64_t p : dst_ptrs) d.push_back(reinterpret_cast<void*>(p));
   run_kv_copy(s.ptrs, d, s.num_blocks, dst_num_blocks, s.block_bytes, s.device, src_block_ids,
-              dst_block_ids, method, bad_pairs, op);
+              dst_block_ids, method, bad_pairs, max_ctas, wait_limit_ns, op);
 }
 
 // out[l, j] = caches[l][block_ids[j]]; out is [L, n, ...] on the caches'
@@ -605,16 +654,20 @@ PYBIND11_MODULE(_C, m) {
   auto kv = m.def_submodule("kv_transfer_ops");
   kv.def("copy_blocks_p2p", &copy_blocks_p2p,
          "Copy KV blocks src_block_ids of src_caches onto dst_block_ids of dst_caches "
-         "(per-layer caches, possibly on different GPUs; pull on the destination GPU by default).",
+         "(per-layer caches, possibly on different GPUs; pull on the destination GPU by default). "
+         "method: 0 auto, 1 SIMT, 2 bulk (needs bad_pairs), 3 copy engines (host ids, no SM); "
+         "max_ctas > 0 caps the kernel's CTAs; wait_limit_ns bounds the bulk method's waits.",
          py::arg("src_caches"), py::arg("dst_caches"), py::arg("src_block_ids"),
          py::arg("dst_block_ids"), py::arg("method") = 0, py::arg("push") = false,
-         py::arg("bad_pairs") = py::none());
+         py::arg("bad_pairs") = py::none(), py::arg("max_ctas") = 0, py::arg("wait_limit_ns") = 0);
   kv.def("copy_blocks_from_ptrs", &copy_blocks_from_ptrs, py::arg("src_ptrs"),
          py::arg("src_num_blocks"), py::arg("dst_caches"), py::arg("src_block_ids"),
-         py::arg("dst_block_ids"), py::arg("method") = 0, py::arg("bad_pairs") = py::none());
+         py::arg("dst_block_ids"), py::arg("method") = 0, py::arg("bad_pairs") = py::none(),
+         py::arg("max_ctas") = 0, py::arg("wait_limit_ns") = 0);
   kv.def("copy_blocks_to_ptrs", &copy_blocks_to_ptrs, py::arg("src_caches"), py::arg("dst_ptrs"),
          py::arg("dst_num_blocks"), py::arg("src_block_ids"), py::arg("dst_block_ids"),
-         py::arg("method") = 0, py::arg("bad_pairs") = py::none());
+         py::arg("method") = 0, py::arg("bad_pairs") = py::none(), py::arg("max_ctas") = 0,
+         py::arg("wait_limit_ns") = 0);
   kv.def("gather_blocks", &gather_blocks, py::arg("caches"), py::arg("block_ids"), py::arg("out"),
          py::arg("bad_ids") = py::none());
   kv.def("scatter_blocks", &scatter_blocks, py::arg("src"), py::arg("caches"),

@@ -152,35 +152,96 @@ class ImportedCaches:
         self.close()
 
 
+# Copy methods of promote()/push(): the SM kernels of pace_kv_copy_blocks, and
+# the copy engines (pace_kv_copy_blocks_ce), which use no SM of either GPU.
+METHOD_AUTO, METHOD_SIMT, METHOD_BULK, METHOD_COPY_ENGINE = 0, 1, 2, 3
+
+
+class KVCopyError(RuntimeError):
+    """A promotion copy skipped pairs or one of its waits expired."""
+
+
+def check_copy_status(counter: torch.Tensor) -> None:
+    """Synchronise with the copy that `counter` belongs to and raise KVCopyError
+    if it counted out-of-range pairs or flagged an expired wait (bit 30) or a
+    load still in flight after the drain (bit 29)."""
+    v = int(counter.item())
+    if v == 0:
+        return
+    timeout = bool(v & (1 << 30))
+    drain = bool(v & (1 << 29))
+    bad = v & ((1 << 29) - 1)
+    parts = []
+    if bad:
+        parts.append(f"{bad} block pair(s) out of range were skipped")
+    if timeout:
+        parts.append("a bounded wait expired, the copy is incomplete")
+    if drain:
+        parts.append("a load was still in flight after the drain; do not trust this device")
+    raise KVCopyError("KV block copy: " + "; ".join(parts))
+
+
+def _counter(dev: torch.device, bad_pairs: Optional[torch.Tensor]) -> torch.Tensor:
+    if bad_pairs is not None:
+        return bad_pairs
+    return torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+def _ids_for(method: int, ids, dev: torch.device):
+    # the copy-engine path reads host ids; the kernels read device ids
+    if method == METHOD_COPY_ENGINE:
+        if isinstance(ids, torch.Tensor):
+            return ids.to(device="cpu", dtype=torch.int32)
+        return torch.tensor(list(ids), dtype=torch.int32)
+    return _ids_tensor(ids, dev)
+
+
 def promote(src, dst_caches: Sequence[torch.Tensor], src_block_ids, dst_block_ids,
-            method: int = 0, bad_pairs: Optional[torch.Tensor] = None) -> None:
+            method: int = METHOD_AUTO, bad_pairs: Optional[torch.Tensor] = None,
+            max_ctas: int = 0, wait_limit_ns: int = 0) -> torch.Tensor:
     """Pull blocks src_block_ids of `src` into dst_block_ids of `dst_caches`,
     on the destination GPU's current stream.  `src` is either a list of
-    per-layer tensors (any GPU of this process) or an ImportedCaches."""
+    per-layer tensors (any GPU of this process) or an ImportedCaches.
+
+    method: METHOD_SIMT / METHOD_BULK run a kernel on the destination GPU
+    (max_ctas > 0 caps its CTAs, leaving SMs to the serving instance);
+    METHOD_COPY_ENGINE queues copies on the copy engines and uses no SM.
+    Returns the int32 counter of skipped pairs and wait flags (`bad_pairs`, or
+    a new one), which check_copy_status() reads after the copy."""
     dev = dst_caches[0].device
-    s = _ids_tensor(src_block_ids, dev)
-    d = _ids_tensor(dst_block_ids, dev)
+    s = _ids_for(method, src_block_ids, dev)
+    d = _ids_for(method, dst_block_ids, dev)
+    bad = _counter(dev, bad_pairs)
     if isinstance(src, ImportedCaches):
         with torch.cuda.device(dev):
             kv_ops.copy_blocks_from_ptrs(src.ptrs, src.num_blocks, list(dst_caches), s, d, method,
-                                         bad_pairs)
+                                         bad, max_ctas, wait_limit_ns)
     else:
-        kv_ops.copy_blocks_p2p(list(src), list(dst_caches), s, d, method, False, bad_pairs)
+        kv_ops.copy_blocks_p2p(list(src), list(dst_caches), s, d, method, False, bad, max_ctas,
+                               wait_limit_ns)
+    return bad
 
 
-def push(src_caches: Sequence[torch.Tensor], dst, src_block_ids, dst_block_ids, method: int = 0,
-         bad_pairs: Optional[torch.Tensor] = None) -> None:
+def push(src_caches: Sequence[torch.Tensor], dst, src_block_ids, dst_block_ids,
+         method: int = METHOD_AUTO, bad_pairs: Optional[torch.Tensor] = None, max_ctas: int = 0,
+         wait_limit_ns: int = 0) -> torch.Tensor:
     """Push blocks from this process's caches into `dst` (ImportedCaches of the
-    receiving worker, or tensors), on the source GPU's current stream."""
+    receiving worker, or tensors), on the source GPU's current stream.  The
+    kernel (or the copy engines) of the source GPU does the work, so the
+    receiving GPU's SMs stay free for serving.  Returns the counter, as
+    promote() does."""
     dev = src_caches[0].device
-    s = _ids_tensor(src_block_ids, dev)
-    d = _ids_tensor(dst_block_ids, dev)
+    s = _ids_for(method, src_block_ids, dev)
+    d = _ids_for(method, dst_block_ids, dev)
+    bad = _counter(dev, bad_pairs)
     if isinstance(dst, ImportedCaches):
         with torch.cuda.device(dev):
             kv_ops.copy_blocks_to_ptrs(list(src_caches), dst.ptrs, dst.num_blocks, s, d, method,
-                                       bad_pairs)
+                                       bad, max_ctas, wait_limit_ns)
     else:
-        kv_ops.copy_blocks_p2p(list(src_caches), list(dst), s, d, method, True, bad_pairs)
+        kv_ops.copy_blocks_p2p(list(src_caches), list(dst), s, d, method, True, bad, max_ctas,
+                               wait_limit_ns)
+    return bad
 
 
 def pair_ranks(world_size: int) -> List[tuple]:
@@ -267,7 +328,12 @@ class KVhelper:
     def export_cache(self) -> CacheExport:
         return export_caches(self.gpu_cache[: self.num_layers])
 
-    def promote_from(self, source, src_block_ids, dst_block_ids, method: int = 0) -> None:
+    def promote_from(self, source, src_block_ids, dst_block_ids, method: int = METHOD_AUTO,
+                     max_ctas: int = 0) -> None:
         """Copy a promoted request's blocks from `source` (an ImportedCaches of the
-        LP worker or its tensors) into this worker's blocks dst_block_ids."""
-        promote(source, self.gpu_cache[: self.num_layers], src_block_ids, dst_block_ids, method)
+        LP worker or its tensors) into this worker's blocks dst_block_ids, and
+        wait for it (like get_kv_cache/insert_kv_cache).  Raises KVCopyError if
+        pairs were out of range or a wait expired."""
+        bad = promote(source, self.gpu_cache[: self.num_layers], src_block_ids, dst_block_ids,
+                      method, max_ctas=max_ctas)
+        check_copy_status(bad)

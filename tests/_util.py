@@ -55,12 +55,22 @@ _REF_CACHE = {}
 
 
 def ref_ops(name: str):
-    """The reference's own CUDA module from oracle/_ref, or None if not built."""
-    if name not in _REF_CACHE:
-        try:
-            from oracle.build_ref import load_ref_ops
+    """The reference's own CUDA module, built from its sources into oracle/_ref.
 
-            _REF_CACHE[name] = load_ref_ops(name)
-        except Exception:
-            _REF_CACHE[name] = None
+    On a machine with a CUDA GPU the module must load: a missing or broken
+    build raises, so a GPU run can never pass with the comparisons against the
+    reference silently skipped.  Without a GPU (where no GPU test runs) it
+    returns None when the module is unavailable."""
+    if name not in _REF_CACHE:
+        from oracle.build_ref import load_ref_ops
+
+        try:
+            mod = load_ref_ops(name)
+            err = None if mod is not None else "not built (oracle/_ref is missing it)"
+        except Exception as exc:  # noqa: BLE001 - reported below with its cause
+            mod, err = None, f"{type(exc).__name__}: {exc}"
+        if mod is None and torch.cuda.is_available():
+            raise RuntimeError(f"reference op module {name!r} cannot be loaded: {err}; "
+                               "build it with `python oracle/build_ref.py <reference root>`")
+        _REF_CACHE[name] = mod
     return _REF_CACHE[name]

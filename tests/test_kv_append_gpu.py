@@ -112,6 +112,71 @@ def test_append_bad_tokens_skipped_and_counted():
                                                                           device=DEV))
 
 
+@pytest.mark.parametrize("form", ["indices", "indptr"])
+@pytest.mark.parametrize("last_len", [17, 0, -3])
+def test_append_inconsistent_last_page_len_is_skipped(form, last_len):
+    """kv_last_page_len outside [1, page_size] makes a request's length disagree
+    with its page count; its tokens must be counted, never written (in the
+    unchecked case position 20 would select kv_indices[p0 + 1], the next
+    request's page)."""
+    nkv, hd, P, ps = 8, 128, 8, 16
+    rng = np.random.default_rng(3)
+    ai = torch.tensor([0, 2, 3], dtype=torch.int32)
+    kp = torch.tensor([0, 1, 2], dtype=torch.int32)        # one page per request
+    ki = torch.tensor([5, 6], dtype=torch.int32)
+    kl = torch.tensor([last_len, 4], dtype=torch.int32)   # request 0 inconsistent
+    key = torch.from_numpy(rng.standard_normal((3, nkv * hd)).astype(np.float32)).bfloat16()
+    value = torch.from_numpy(rng.standard_normal((3, nkv * hd)).astype(np.float32)).bfloat16()
+    cache = torch.zeros(P, 2, ps, nkv, hd).bfloat16()
+    if form == "indices":
+        bi = torch.tensor([0, 0, 1], dtype=torch.int32)
+        pos = torch.tensor([15, 16, 3], dtype=torch.int32)
+    else:
+        b_, p_ = append_ref.batch_indices_positions_checked(ai, kp, kl, ps, 3)
+        bi, pos = torch.tensor(b_, dtype=torch.int32), torch.tensor(p_, dtype=torch.int32)
+    want, nbad = append_ref.append_paged_kv_cache_checked(key, value, bi, pos, cache.clone(), ki,
+                                                          kp, kl)
+    assert nbad >= 1
+    got = cache.to(DEV)
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    if form == "indices":
+        kv.append_paged_kv_cache(key.to(DEV), value.to(DEV), bi.to(DEV), pos.to(DEV), got,
+                                 ki.to(DEV), kp.to(DEV), kl.to(DEV), "NHD", bad)
+    else:
+        kv.append_paged_kv_cache_by_indptr(key.to(DEV), value.to(DEV), ai.to(DEV), got, ki.to(DEV),
+                                           kp.to(DEV), kl.to(DEV), bad)
+    torch.cuda.synchronize()
+    assert bad.item() == nbad
+    assert torch.equal(got.cpu(), want)
+    assert torch.equal(got[6, 0, 3].cpu(), key[2].view(nkv, hd))  # the valid request landed
+
+
+def test_append_indptr_not_starting_at_zero_is_skipped():
+    """append_indptr[0] > 0: tokens before it belong to no request and are
+    counted; the kernel must not place them inside request 0's window."""
+    nkv, hd, P, ps = 8, 128, 8, 16
+    ai = torch.tensor([2, 4], dtype=torch.int32)   # tokens 0 and 1 are uncovered
+    kp = torch.tensor([0, 2], dtype=torch.int32)
+    ki = torch.tensor([1, 4], dtype=torch.int32)
+    kl = torch.tensor([9], dtype=torch.int32)      # length 25
+    key = torch.randn(4, nkv * hd).bfloat16()
+    value = torch.randn(4, nkv * hd).bfloat16()
+    cache = torch.zeros(P, 2, ps, nkv, hd).bfloat16()
+    b_, p_ = append_ref.batch_indices_positions_checked(ai, kp, kl, ps, 4)
+    assert b_ == [-1, -1, 0, 0] and p_[2:] == [23, 24]
+    want, nbad = append_ref.append_paged_kv_cache_checked(
+        key, value, torch.tensor(b_, dtype=torch.int32), torch.tensor(p_, dtype=torch.int32),
+        cache.clone(), ki, kp, kl)
+    assert nbad == 2
+    got = cache.to(DEV)
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kv.append_paged_kv_cache_by_indptr(key.to(DEV), value.to(DEV), ai.to(DEV), got, ki.to(DEV),
+                                       kp.to(DEV), kl.to(DEV), bad)
+    torch.cuda.synchronize()
+    assert bad.item() == 2
+    assert torch.equal(got.cpu(), want)
+
+
 def test_append_through_c_abi():
     lib = cabi.load()
     rng = np.random.default_rng(9)

@@ -30,7 +30,7 @@ def run_topk(gating: torch.Tensor, k: int, renormalize=False):
 
 @pytest.mark.parametrize("E,k", [(8, 2), (8, 1), (16, 4), (64, 6), (128, 8), (256, 8), (4, 2),
                                  (2, 1), (1, 1), (60, 4), (160, 6), (7, 2)])
-@pytest.mark.parametrize("T", [1, 64, 4096])
+@pytest.mark.parametrize("T", [1, 64, 512, 4096, 16384])
 def test_topk_softmax(T, E, k):
     g = torch.randn(T, E, generator=torch.Generator().manual_seed(T * 31 + E))
     w, ids, tei = run_topk(g, k)

@@ -109,7 +109,10 @@ def test_fused_add_matches_composition():
 
 
 def _golden_files():
-    return sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+    """Fixtures produced by the reference's CUDA ops (make_golden.py); the
+    wrapper-call recording (wrapper_calls.npz) has its own tests."""
+    return sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
+                  if os.path.basename(p) != "wrapper_calls.npz")
 
 
 @pytest.mark.skipif(not _golden_files(), reason="no golden vectors committed yet")
@@ -183,3 +186,29 @@ def test_config1_chain_properties():
     act64 = a64 / (1 + torch.exp(-a64)) * b64
     assert (out["act"].double() - act64).abs().max().item() <= 1e-5 * act64.abs().max().item()
     assert ops_ref.CONFIG1_BYTES_PER_TOKEN == 279048
+
+
+def test_append_checked_rule_rejects_inconsistent_metadata():
+    """The invalid-metadata rule of the append (skip and count): a last-page
+    length of page_size + 1, an uncovered token (append_indptr[0] > 0) and an
+    out-of-range page are counted and leave the cache untouched."""
+    from oracle import append_ref
+
+    ps, heads, hd = 16, 2, 8
+    cache = torch.zeros(6, 2, ps, heads, hd)
+    key = torch.randn(3, heads * hd)
+    value = torch.randn(3, heads * hd)
+    kp = torch.tensor([0, 1, 3])
+    ki = torch.tensor([2, 4, 9])          # request 1's second page (9) is out of range
+    kl = torch.tensor([ps + 1, 5])        # request 0 inconsistent: 1 page, length 17
+    assert append_ref.token_slot(0, 16, ki, kp, kl, ps, 6) is None
+    assert append_ref.token_slot(1, 3, ki, kp, kl, ps, 6) == (4, 3)
+    assert append_ref.token_slot(1, 20, ki, kp, kl, ps, 6) is None  # page 9
+    got, bad = append_ref.append_paged_kv_cache_checked(
+        key, value, torch.tensor([0, 1, 1]), torch.tensor([16, 3, 20]), cache.clone(), ki, kp, kl)
+    assert bad == 2
+    assert torch.equal(got[4, 0, 3], key[1].view(heads, hd))
+    assert int(got.ne(0).sum()) == 2 * heads * hd
+    bi, pos = append_ref.batch_indices_positions_checked(torch.tensor([1, 2, 3]), kp,
+                                                         torch.tensor([4, 5]), ps, 3)
+    assert bi == [-1, 0, 1] and pos[1:] == [3, 20]
