@@ -54,6 +54,7 @@ B_ROPE = 4 * (NQ + NKV) * HD * T + T * HD * 4 + 8 * T
 B_SILU = 6 * I * T
 B_STEP = B_RMS + B_ROPE + B_FUSED + B_SILU + (L - 1) * (B_FUSED + B_ROPE + B_FUSED + B_SILU)
 LAUNCHES_PER_STEP = 4 * L
+TIMED_BLOCKS = 5  # timed blocks of K steps each; the line reports the median block
 
 WORKLOAD = (
     "Llama-3-8B 32-layer op chain (rms_norm/fused_add_rms_norm, neox rope 32/8x128 fp32 cache, "
@@ -255,6 +256,41 @@ def time_replays(g, steps, warmup, sampler=None) -> float:
     return e0.elapsed_time(e1)
 
 
+def time_blocks(g, steps, warmup, blocks, sampler=None, ws=1):
+    """Milliseconds of each of `blocks` timed blocks of exactly `steps` graph
+    replays, after `warmup` replays.  Each block is bracketed by a barrier (N > 1)
+    and a device synchronisation, timed with CUDA events on the replay stream,
+    and reduced to the max over ranks."""
+    import torch
+
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    ctx = sampler if sampler is not None else _Null()
+    out = []
+    with ctx:
+        for _ in range(blocks):
+            if ws > 1:
+                import torch.distributed as dist
+
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                g.replay()
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            if ws > 1:
+                t = torch.tensor([ms], device="cuda")
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = t.item()
+            out.append(ms)
+    return out
+
+
 class _Null:
     def __enter__(self):
         return self
@@ -361,11 +397,79 @@ def e2e_chain(chs, ops, steps, warmup, ws=1):
                     "next step's ops"}
 
 
+def e2e_breakdown(chs, ops, steps, warmup, ws=1):
+    """What limits the e2e number: the same eager chain with no host copies
+    (launch_only: the host's pybind -> C-ABI calls and the GPU work), and the
+    host copies alone with no ops (copies_only: the same H2D/D2H bytes per step
+    on the copy streams).  Each timed like e2e (events, max over ranks)."""
+    import torch
+
+    dev = chs[0]["positions"].device
+    comp = torch.cuda.current_stream()
+    h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
+    h_pos = [c["positions"].cpu().pin_memory() for c in chs]
+    h_hidden = [c["layers"][0]["hidden"].cpu().pin_memory() for c in chs]
+    h_out = [torch.empty(T, I, dtype=torch.bfloat16, pin_memory=True) for _ in chs]
+
+    def timed(step):
+        for i in range(warmup):
+            step(i)
+        torch.cuda.synchronize(dev)
+        if ws > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record(comp)
+        h2d_s.wait_event(e0)
+        d2h_s.wait_event(e0)
+        for i in range(steps):
+            step(i)
+        host_ms = (time.perf_counter() - t0) * 1e3 / steps
+        comp.wait_stream(h2d_s)
+        comp.wait_stream(d2h_s)
+        e1.record(comp)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        if ws > 1:
+            t = torch.tensor([ms, host_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, host_ms = t[0].item(), t[1].item()
+        return ms, host_ms
+
+    def launches(i):
+        run_chain(chs[i % len(chs)], ops)
+
+    def copies(i):
+        k = i % len(chs)
+        with torch.cuda.stream(h2d_s):
+            chs[k]["positions"].copy_(h_pos[k], non_blocking=True)
+            chs[k]["layers"][0]["hidden"].copy_(h_hidden[k], non_blocking=True)
+        with torch.cuda.stream(d2h_s):
+            h_out[k].copy_(chs[k]["layers"][-1]["act"], non_blocking=True)
+
+    ms_l, host_l = timed(launches)
+    ms_c, _ = timed(copies)
+    nbytes = h_pos[0].numel() * 8 + h_hidden[0].numel() * 2 + h_out[0].numel() * 2
+    return {"launch_only": {"ms_per_step": round(ms_l, 4), "value": round(ws * T / (ms_l * 1e-3), 1),
+                            "host_ms_per_step": round(host_l, 4),
+                            "host_us_per_call": round(host_l * 1e3 / LAUNCHES_PER_STEP, 3)},
+            "copies_only": {"ms_per_step": round(ms_c, 4), "bytes_per_step": nbytes,
+                            "gbs_per_gpu": round(nbytes / (ms_c * 1e-3) / 1e9, 1)},
+            "steps": steps}
+
+
 # ------------------------------------------------------------ CPU oracle --
-def cpu_chain_sample(budget_s: float = 8.0, max_passes: int = 1 << 30, warmup: int = 1):
-    """The reference formulas (oracle port) on the host cores: time one input-norm
-    layer-0 pass and repeated layer>=1 passes at T=512 bf16 (at most `max_passes`,
-    stopping after `budget_s` seconds), scale to 32 layers."""
+def cpu_chain_run(steps: int, warmup: int, budget_s: float):
+    """The reference's formulas (the oracle port) on the host cores, `steps` timed
+    steps after `warmup`: a step is one pass of the 32-layer op chain at T=512
+    bf16 (layer 0: rms_norm; layers 1..31: fused_add_rms_norm, rope,
+    fused_add_rms_norm, silu_and_mul), all host threads.  When `steps` full
+    chains would take longer than `budget_s`, each step is a bounded sample of
+    the first layers of the chain, scaled to 32 layers (stated in `sample`)."""
     import torch
 
     from oracle import ops_ref
@@ -382,22 +486,28 @@ def cpu_chain_sample(budget_s: float = 8.0, max_passes: int = 1 << 30, warmup: i
             "w_post": rn(H, mean=1, std=0.02), "gate_up": rn(T, 2 * I)}
     pos = make_positions(g, "cpu")
     cache = rope_cache("cpu")
-    for _ in range(max(1, warmup)):
-        ops_ref.chain_layer(1, dict(bufs), cache, pos, EPS, NQ, NKV, HD)
+
+    def chain(layers: int):
+        for layer in range(layers):
+            ops_ref.chain_layer(0 if layer == 0 else 1, bufs, cache, pos, EPS, NQ, NKV, HD)
+
     t0 = time.perf_counter()
-    ops_ref.chain_layer(0, dict(bufs), cache, pos, EPS, NQ, NKV, HD)
-    t_l0 = time.perf_counter() - t0
-    n, t_sum = 0, 0.0
-    while n < 2 or (t_sum < budget_s and n < max_passes):
-        t0 = time.perf_counter()
-        ops_ref.chain_layer(1, bufs, cache, pos, EPS, NQ, NKV, HD)
-        t_sum += time.perf_counter() - t0
-        n += 1
-    t_l = t_sum / n
-    step_s = t_l0 + (L - 1) * t_l
-    return {"value": round(T / step_s, 1), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"T=512 bf16 op chain on CPU (torch, {cores} threads): 1 layer-0 pass + "
-                      f"{n} layer>=1 passes ({t_sum:.1f} s), scaled to 32 layers"}
+    chain(L)  # the first full chain also sizes the steps
+    t_full = time.perf_counter() - t0
+    layers = L
+    if (steps + max(0, warmup - 1)) * t_full > budget_s:
+        layers = max(1, int(L * budget_s / ((steps + max(0, warmup - 1)) * t_full)))
+    for _ in range(max(0, warmup - 1)):
+        chain(layers)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        chain(layers)
+    dt = (time.perf_counter() - t0) / steps * (L / layers)
+    what = "the full 32-layer chain" if layers == L else f"the first {layers} of 32 layers, scaled to 32"
+    return {"value": round(T / dt, 1), "unit": UNIT, "cores": cores, "kind": "port",
+            "ms_per_step": round(dt * 1e3, 3), "steps_timed": steps,
+            "sample": f"T=512 bf16 op chain on the host CPU (torch, {cores} threads), {steps} timed "
+                      f"steps after {warmup} warm-up, each step {what}"}
 
 
 def cpu_config1_sample(budget_s: float = 3.0):
@@ -590,11 +700,24 @@ def _overlap_chain(dev, copies, nbytes, reps):
     return out
 
 
+# Promotion paths measured beside the serving chain: (side, method, max_ctas).
+# "pull" runs on the HP (serving) GPU, "push" on the LP GPU; method 3 is the
+# copy engines (no SM); max_ctas caps the kernel's CTAs.
+KV_PATHS = {
+    "pull_simt": ("pull", 1, 0),
+    "pull_simt_16ctas": ("pull", 1, 16),
+    "pull_bulk": ("pull", 2, 0),
+    "pull_copy_engine": ("pull", 3, 0),
+    "push_simt": ("push", 1, 0),
+    "push_copy_engine": ("push", 3, 0),
+}
+
+
 def kv_overlap(dev, reps: int = 100):
     """Promotion while serving, on one GPU: the 32-layer chain (a CUDA graph) on
     the main stream and the promotion copy (1.1 GB, HBM -> HBM) on a side
-    stream at the same time.  Per copy method: the chain's ms per step and the
-    copy's GB/s, alone and concurrent."""
+    stream at the same time.  Per copy path: the chain's ms per step and the
+    copy's GB/s, alone and concurrent; each path's copy checked byte-exact."""
     import torch
 
     from paceserve_b200 import kv_transfer as kvt
@@ -604,17 +727,135 @@ def kv_overlap(dev, reps: int = 100):
     dc = _kv_caches(dev)
     sids = torch.tensor(src, dtype=torch.int32, device=dev)
     dids = torch.tensor(dst, dtype=torch.int32, device=dev)
+    sids_h, dids_h = sids.cpu(), dids.cpu()
     nbytes = len(src) * KV_L * KV_BLOCK_BYTES
-    copies = {name: (lambda m=m: kvt.promote(sc, dc, sids, dids, method=m))
-              for m, name in KV_METHODS.items()}
-    return _overlap_chain(dev, copies, nbytes, reps)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    copies, exact = {}, {}
+    for name, (_side, m, ctas) in KV_PATHS.items():
+        if name.startswith("push"):
+            continue  # one GPU: push and pull are the same copy
+        ids = (sids_h, dids_h) if m == 3 else (sids, dids)
+        fn = (lambda m=m, ctas=ctas, ids=ids: kvt.promote(sc, dc, ids[0], ids[1], method=m,
+                                                        bad_pairs=bad, max_ctas=ctas))
+        for c in dc:
+            c[dids.long()] = 0
+        fn()
+        torch.cuda.synchronize()
+        exact[name] = bool(all(torch.equal(dc[l][dids.long()], sc[l][sids.long()])
+                               for l in range(KV_L))) and bad.item() == 0
+        copies[name] = fn
+    out = _overlap_chain(dev, copies, nbytes, reps)
+    for name in copies:
+        out[name]["byte_exact"] = exact[name]
+    return out
+
+
+def _pair_overlap(role, pair_lp, pair_hp, imported, caches, peer_caches, sids, dids, nbytes,
+                  g_ref, dev, reps=60):
+    """Promotion while serving across a pair: the HP GPU replays the 32-layer
+    chain while the promotion runs by each path of KV_PATHS (pull on the HP GPU
+    or push from the LP GPU, by SM kernel or copy engine).  Every rank takes the
+    same collective steps.  Returns {path: result} on HP ranks, None elsewhere."""
+    import torch
+    import torch.distributed as dist
+
+    import paceserve_b200 as pb
+    from paceserve_b200 import kv_transfer as kvt
+
+    ops = (pb.layernorm_ops, pb.pos_encoding_ops, pb.activation_ops)
+    g = chain_ms = None
+    if role == "hp":
+        ch = build_chain(dev, seed=5)
+        g = capture(lambda: run_chain(ch, ops))
+        chain_ms = time_replays(g, reps, 5) / reps
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    sids_h = sids.cpu() if sids is not None else None
+    dids_h = dids.cpu() if dids is not None else None
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    results = {}
+    for name, (where, m, ctas) in KV_PATHS.items():
+        mine = role == ("hp" if where == "pull" else "lp")
+        fn = None
+        if mine:
+            ids = (sids_h, dids_h) if m == 3 else (sids, dids)
+            if where == "pull":
+                fn = (lambda m=m, ctas=ctas, ids=ids: kvt.promote(
+                    imported, caches, ids[0], ids[1], method=m, bad_pairs=bad, max_ctas=ctas))
+            else:
+                fn = (lambda m=m, ctas=ctas, ids=ids: kvt.push(
+                    caches, peer_caches, ids[0], ids[1], method=m, bad_pairs=bad, max_ctas=ctas))
+        # 1. byte-exactness of this path: clear the targets, copy once, compare
+        if role == "hp":
+            for c in caches:
+                c[dids.long()] = 0
+            torch.cuda.synchronize()
+        dist.barrier()
+        bad.zero_()
+        if fn is not None:
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ok = None
+        if role == "hp":
+            ok = bool(torch.equal(torch.stack([c[dids.long()] for c in caches]), g_ref))
+        # 2. the copy alone
+        copy_ms = 0.0
+        if fn is not None:
+            with torch.cuda.stream(side):
+                copy_ms = _time_copy(fn, 5, 2)
+        info = [None] * dist.get_world_size()
+        dist.all_gather_object(info, (role, copy_ms, int(bad.item()), chain_ms or 0.0))
+        # 3. both at once: the chain on HP, as many copies on the side that runs
+        # them as fill the chain's time
+        n_copy = 0
+        if fn is not None and copy_ms > 0:
+            hp_chain = chain_ms if role == "hp" else info[pair_hp][3]
+            n_copy = max(1, round(reps * hp_chain / copy_ms))
+        dist.barrier()
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(main)
+        ev[2].record(side)
+        for i in range(max(reps if role == "hp" else 0, n_copy if fn is not None else 0)):
+            if role == "hp" and i < reps:
+                g.replay()
+            if fn is not None and i < n_copy:
+                with torch.cuda.stream(side):
+                    fn()
+        ev[1].record(main)
+        ev[3].record(side)
+        torch.cuda.synchronize()
+        c_ms = ev[0].elapsed_time(ev[1]) / reps if role == "hp" else 0.0
+        k_ms = ev[2].elapsed_time(ev[3]) / n_copy if (fn is not None and n_copy) else 0.0
+        res = [None] * dist.get_world_size()
+        dist.all_gather_object(res, (role, c_ms, k_ms, ok, int(bad.item())))
+        if role == "hp":
+            copy_ms_pair = copy_ms if mine else info[pair_lp][1]
+            peer_k = k_ms if mine else res[pair_lp][2]
+            peer_bad = int(bad.item()) if mine else res[pair_lp][4]
+            results[name] = {
+                "runs_on": "HP GPU" if where == "pull" else "LP GPU",
+                "engine": "copy engines" if m == 3 else ("SM kernel, %s" % (
+                    f"{ctas} CTAs" if ctas else "all SMs")),
+                "byte_exact": bool(ok) and peer_bad == 0,
+                "copy_gbs_alone": round(nbytes / (copy_ms_pair * 1e-3) / 1e9, 1),
+                "chain_ms_concurrent": round(c_ms, 4),
+                "chain_slowdown": round(c_ms / chain_ms - 1, 4),
+                "copy_gbs_concurrent": round(nbytes / (peer_k * 1e-3) / 1e9, 1) if peer_k else None}
+    if g is not None:
+        del g
+    return ({"chain_ms_alone": round(chain_ms, 4), "copy_bytes": nbytes, "paths": results}
+            if role == "hp" else None)
 
 
 def kv_promotion(ws, rank, local, steps, warmup, baseline=True, overlap=False):
     """LP->HP promotion on rank pairs (0->1, 2->3, ...): the HP rank pulls the
-    request blocks from the LP rank's caches (CUDA IPC) with one kernel.  With one
-    GPU, LP and HP caches both live on it (an HBM-to-HBM copy).  Returns the
-    result dict on every rank (collectives are taken by all ranks in the same order)."""
+    request blocks from the LP rank's caches (CUDA IPC) with one kernel per
+    method.  With one GPU, LP and HP caches both live on it (an HBM-to-HBM copy).
+    overlap=True adds, on every pair, the chain's slowdown while a promotion runs
+    by each path of KV_PATHS.  Returns the result dict on every rank
+    (collectives are taken by all ranks in the same order)."""
     import torch
 
     from paceserve_b200 import kv_transfer as kvt
@@ -622,6 +863,7 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True, overlap=False):
     dev = torch.device(f"cuda:{local}")
     out = {"workload": f"LP->HP KV promotion, Llama-3-8B paged cache [{KV_NB}, 2, 16, 8, 128] bf16 x "
                        "32 layers, 8 requests lognormal(6.9, 0.7) capped 8192, 80 % occupied"}
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
     if ws == 1:
         lens, src, dst = kv_requests(7)
         sc = _kv_caches(dev, fill_seed=100)
@@ -631,12 +873,13 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True, overlap=False):
         nbytes = len(src) * KV_L * KV_BLOCK_BYTES
         res = {}
         for m, name in KV_METHODS.items():
-            ms = _time_copy(lambda: kvt.promote(sc, dc, sids, dids, method=m), steps, warmup)
+            ms = _time_copy(lambda: kvt.promote(sc, dc, sids, dids, method=m, bad_pairs=bad), steps,
+                            warmup)
             res[name] = {"ms": round(ms, 4), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
                          "hbm_gbs": round(2 * nbytes / (ms * 1e-3) / 1e9, 1)}
         ok = all(torch.equal(dc[l][dids.long()], sc[l][sids.long()]) for l in range(KV_L))
         out.update({"mode": "one GPU: HBM -> HBM", "blocks": int(len(src)), "bytes": nbytes,
-                    "byte_exact": bool(ok), "methods": res})
+                    "byte_exact": bool(ok) and bad.item() == 0, "methods": res})
         out["host_path"] = kv_host_path(sc, dc, sids, dids, max(2, steps // 4), 2)
         if baseline:
             d2h, h2d = kv_reference_path(sc, dc, src, dst, dev)
@@ -658,41 +901,49 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True, overlap=False):
         caches = _kv_caches(dev, fill_seed=100 + mine[0])
     elif role == "hp":
         caches = _kv_caches(dev)
-    exports = kvt.exchange_exports(kvt.export_caches(caches) if role == "lp" else None)
+    # both sides export: the HP rank pulls from the LP caches, the LP rank pushes
+    # into the HP caches
+    exports = kvt.exchange_exports(kvt.export_caches(caches) if role is not None else None)
     times = {m: 0.0 for m in KV_METHODS}
     nbytes, nblocks, imported = 0, 0, None
+    sids = dids = None
     if mine is not None:
         lens, src, dst = kv_requests(7)  # the same promotion on every pair
         nblocks = len(src)
         nbytes = nblocks * KV_L * KV_BLOCK_BYTES
-    dist.barrier()
-    if role == "hp":
-        imported = kvt.ImportedCaches(exports[mine[1]], local)
         sids = torch.tensor(src, dtype=torch.int32, device=dev)
         dids = torch.tensor(dst, dtype=torch.int32, device=dev)
+        imported = kvt.ImportedCaches(exports[mine[2] if role == "lp" else mine[1]], local)
+    dist.barrier()
+    if role == "hp":
         for m in KV_METHODS:
-            times[m] = _time_copy(lambda: kvt.promote(imported, caches, sids, dids, method=m),
-                                  steps, warmup)
+            times[m] = _time_copy(lambda: kvt.promote(imported, caches, sids, dids, method=m,
+                                                      bad_pairs=bad), steps, warmup)
     t = torch.tensor([times[m] for m in KV_METHODS], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ok = True
+    g_ref = None
     if role == "lp":
-        g = torch.stack([c[torch.tensor(src, device=dev)] for c in caches])
+        g = torch.stack([c[sids.long()] for c in caches])
         dist.send(g, dst=mine[2])
         del g
     elif role == "hp":
-        g = torch.empty(KV_L, nblocks, *KV_SLAB, dtype=torch.bfloat16, device=dev)
-        dist.recv(g, src=mine[1])
-        ok = bool(torch.equal(torch.stack([c[dids.long()] for c in caches]), g))
-        del g
-        if overlap:
-            # Promotion while serving: the HP GPU runs the chain while pulling.
-            copies = {name: (lambda m=m: kvt.promote(imported, caches, sids, dids, method=m))
-                      for m, name in KV_METHODS.items()}
-            out_overlap = _overlap_chain(dev, copies, nbytes, 60)
+        g_ref = torch.empty(KV_L, nblocks, *KV_SLAB, dtype=torch.bfloat16, device=dev)
+        dist.recv(g_ref, src=mine[1])
+        ok = bool(torch.equal(torch.stack([c[dids.long()] for c in caches]), g_ref)) and \
+            bad.item() == 0
+    ov = None
+    if overlap:
+        # Promotion while serving: the HP GPU runs the chain while the promotion
+        # runs by each path.
+        ov = _pair_overlap(role, mine[1] if mine else None, mine[2] if mine else None, imported,
+                           caches, imported, sids, dids, nbytes, g_ref, dev)
+    torch.cuda.synchronize()
+    dist.barrier()
+    if imported is not None:
         imported.close()
+    del g_ref
     info = [None] * ws
-    ov = out_overlap if (overlap and role == "hp") else None
     dist.all_gather_object(info, (role, ok, nbytes, [times[m] for m in KV_METHODS], ov))
     dist.barrier()
     hps = [x for x in info if x[0] == "hp"]
@@ -712,7 +963,10 @@ def kv_promotion(ws, rank, local, steps, warmup, baseline=True, overlap=False):
                 "nvlink_frac": round(best["gbs_per_pair"] / NVLINK_GBS, 4),
                 "nvlink_peak_gbs": NVLINK_GBS, "nvlink_peak_source": "measured peer copy on this pool"})
     if overlap:
-        out["overlap_on_hp"] = [x[4] for x in hps]
+        out["promotion_while_serving"] = {
+            "what": "per pair: the HP GPU replays the 32-layer chain while the promotion runs by "
+                    "each path (pull = on the HP GPU, push = from the LP GPU)",
+            "per_pair": [x[4] for x in hps]}
     return out
 
 
@@ -877,19 +1131,23 @@ def init_dist():
     return ws, rank, local
 
 
-def run_reference(args, ws, rank):
-    """Reference arm: each step is one decoder layer of the chain computed by the
-    reference's formulas on the host CPU (bounded sample), scaled to 32 layers."""
+def run_reference(args, rank):
+    """Reference arm: the reference's own formulas for the path (the oracle port;
+    the reference has no CPU implementation of these ops) on the host cores, one
+    process with every host thread, rank 0 only.  A step is one pass of the
+    32-layer op chain at T=512 (bounded as cpu_chain_run says).  Under torchrun
+    the other ranks exit without work: the value is the whole host CPU's rate,
+    the same at every N, comparable to the whole job's rate of the GPU arm."""
     if rank != 0:
         return
-    base = cpu_chain_sample(budget_s=30.0, max_passes=args.steps, warmup=args.warmup)
-    ms = T / base["value"] * 1e3
+    base = cpu_chain_run(args.steps, args.warmup, budget_s=90.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "tokens_per_step": T, "layers": L},
+        "config": {"workload": WORKLOAD, "tokens_per_step": T, "layers": L,
+                   "scope": "whole host CPU: one process, all cores, independent of N"},
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "cpu_config1": cpu_config1_sample(),
@@ -912,6 +1170,28 @@ def run_side_workload(args, ws, rank, local):
             if ws == 1:
                 torch.cuda.empty_cache()
                 line["kv_overlap"] = kv_overlap(dev)
+    elif args.workload == "opgraph":
+        # For a graph-level ncu capture of one op's launches (ncu --graph-profiling
+        # graph): DRAM bytes counted over the whole graph include the write-backs
+        # of each launch's output, which a per-launch capture misses (they leave
+        # L2 after the launch ends).  No eager launch precedes the graph.
+        import paceserve_b200 as pb
+
+        ch = build_chain(dev, seed=1)
+        layers = ch["layers"][: args.layers]
+        act = pb.activation_ops
+        s_ = torch.cuda.Stream()
+        s_.wait_stream(torch.cuda.current_stream())
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s_):
+            for b in layers:
+                act.silu_and_mul(b["act"], b["gate_up"])
+        for _ in range(args.steps):
+            gr.replay()
+        torch.cuda.synchronize()
+        line = {"metric": "silu_and_mul graph replays for a graph-level ncu capture",
+                "launches_per_replay": len(layers), "replays": args.steps,
+                "algorithmic_bytes_per_launch": B_SILU}
     elif args.workload == "sweep":
         line = {"metric": "per-op HBM GB/s, token sweep", "sweep": sweep(dev) if rank == 0 else None,
                 "peak_gbs": peaks()["hbm_gbs"]}
@@ -934,24 +1214,27 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the config-3 sweep and config-4 MoE keys of the N=1 line")
     ap.add_argument("--kv-blocks", type=int, default=8192,
                     help="blocks per layer of the kv workload's caches (a smaller case for ncu)")
-    ap.add_argument("--workload", choices=["chain", "kv", "sweep", "moe"], default="chain",
+    ap.add_argument("--workload", choices=["chain", "kv", "sweep", "moe", "opgraph"],
+                    default="chain",
                     help="chain: the headline op chain (the driver's line); kv: LP->HP "
-                         "promotion; sweep: per-op token sweep; moe: Mixtral-8x7B routing")
+                         "promotion; sweep: per-op token sweep; moe: Mixtral-8x7B routing; "
+                         "opgraph: silu_and_mul graph replays for a graph-level ncu capture")
+    ap.add_argument("--layers", type=int, default=32,
+                    help="opgraph: launches (layers) per graph")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     KV_NB = args.kv_blocks
-    ws, rank, local = init_dist()
-    if args.impl == "ours" and args.workload != "chain":
-        run_side_workload(args, ws, rank, local)
-        return
     if args.impl == "reference":
-        run_reference(args, ws, rank)
-        if ws > 1:
-            import torch.distributed as dist
-
-            dist.destroy_process_group()
+        # host-CPU arm: no process group, no GPU
+        run_reference(args, int(os.environ.get("RANK", "0")))
+        return
+    ws, rank, local = init_dist()
+    if args.workload != "chain":
+        run_side_workload(args, ws, rank, local)
         return
 
     import torch
@@ -969,11 +1252,8 @@ def main():
 
         dist.barrier()
     torch.cuda.synchronize()
-    ms_total = time_replays(g, args.steps, args.warmup, sampler)
-    if ws > 1:
-        t = torch.tensor([ms_total], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = t.item()
+    blocks = time_blocks(g, args.steps, args.warmup, TIMED_BLOCKS, sampler, ws)
+    ms_total = statistics.median(blocks)
     del g
     ms_step = ms_total / args.steps
     value = ws * T * args.steps / (ms_total * 1e-3)
@@ -988,8 +1268,10 @@ def main():
             "frac_of_nominal": round(silu["gbs"] / NOMINAL_HBM_GBS, 4),
             "traffic": ncu_traffic("silu_and_mul_T512"),
             "algorithmic_bytes": B_SILU}
-    e2e = e2e_chain([ch, build_chain(dev, seed=4321 + rank)], ops, steps=min(args.steps, 50),
-                    warmup=3, ws=ws)
+    chs = [ch, build_chain(dev, seed=4321 + rank)]
+    e2e = e2e_chain(chs, ops, steps=min(args.steps, 50), warmup=3, ws=ws)
+    e2e_parts = e2e_breakdown(chs, ops, steps=min(args.steps, 50), warmup=3, ws=ws)
+    del chs
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
@@ -999,23 +1281,39 @@ def main():
                    "parallelism": f"{ws} independent replicas" if ws > 1 else "single GPU",
                    "l2": "distinct per-layer buffers, 2.1 GB per step > 126 MB L2 (no flush)",
                    "graph": "one CUDA graph per step, PDL between kernels"},
+        "timing": {"blocks": TIMED_BLOCKS, "steps_per_block": args.steps,
+                   "ms_per_block": [round(b, 4) for b in blocks],
+                   "reported": "median block (each block: barrier + sync, CUDA events, max over ranks)"},
         "chain_hbm": {"bytes_per_step": B_STEP, "achieved_gbs": round(chain_gbs, 1),
                       "frac": round(chain_gbs / pk["hbm_gbs"], 4),
                       "frac_of_nominal": round(chain_gbs / NOMINAL_HBM_GBS, 4)},
         "roofline": roof,
         "ops": ops_t,
         "e2e": e2e,
+        "e2e_breakdown": e2e_parts,
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "clocks": sampler.summary(),
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_chain_sample()
+        line["cpu_baseline"] = cpu_chain_run(min(args.steps, 20), 1, budget_s=12.0)
         line["cpu_baseline"]["config1"] = cpu_config1_sample()
+    if ws == 1 and not args.no_sweep:
+        del ch
+        torch.cuda.empty_cache()
+        line["sweep"] = {"what": "BASELINE config 3: per-op GB/s, T in {1..16384}, Llama-3-8B and "
+                                 "-70B shapes, bf16 and fp16, 32-launch graphs over distinct "
+                                 "buffers (>= 512 MB per cycle)",
+                         "peak_gbs": pk["hbm_gbs"], "rows": sweep(dev, reps=5)}
+        torch.cuda.empty_cache()
+        line["moe"] = {"what": "BASELINE config 4: Mixtral-8x7B routing, topk_softmax (E=8, top-2, "
+                               "renormalised) + moe_align_block_size (block 64); latency bound",
+                       "rows": moe_routing(dev, reps=50)}
     if ws > 1:
         del ch
         torch.cuda.empty_cache()
         try:
-            line["kv_promotion"] = kv_promotion(ws, rank, local, steps=min(args.steps, 20), warmup=3)
+            line["kv_promotion"] = kv_promotion(ws, rank, local, steps=min(args.steps, 20), warmup=3,
+                                                overlap=True)
         except Exception as exc:  # reported, never fatal for the chain line
             line["kv_promotion"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         dist.barrier()

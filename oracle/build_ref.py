@@ -15,8 +15,8 @@ The resulting ``.so`` files are git-ignored but travel to the GPU box, where
 ``load_ref_ops`` imports them without the reference sources being present.
 
 Usage: ``python oracle/build_ref.py [reference_root]`` (default: the
-``PACE_REFERENCE_ROOT`` environment variable, else ``DEFAULT_REF_ROOT``).
-Skips modules whose ``.so`` is newer than its sources.
+``PACE_REFERENCE_ROOT`` environment variable, else a ``reference`` checkout
+beside this repository).  Skips modules whose ``.so`` is newer than its sources.
 """
 from __future__ import annotations
 
@@ -28,7 +28,9 @@ from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF_ROOT = os.environ.get("PACE_REFERENCE_ROOT", "/root/reference")
+DEFAULT_REF_ROOT = os.environ.get(
+    "PACE_REFERENCE_ROOT",
+    os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 # module name -> reference source files (paths relative to the reference root)
 REF_MODULES = {

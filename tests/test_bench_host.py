@@ -12,9 +12,10 @@ from oracle import append_ref
 def test_reference_arm_json_line(monkeypatch, capsys):
     """`bench.py --impl reference` at N=1: one JSON line with the contract's keys
     (the CPU samples are shortened for the test)."""
-    real_chain, real_cfg1 = bench.cpu_chain_sample, bench.cpu_config1_sample
-    monkeypatch.setattr(bench, "cpu_chain_sample",
-                        lambda budget_s=0.0, max_passes=1, warmup=0: real_chain(0.0, 1, 0))
+    real_chain, real_cfg1 = bench.cpu_chain_run, bench.cpu_config1_sample
+    # one layer per step: the budget scales a step down to a bounded sample
+    monkeypatch.setattr(bench, "cpu_chain_run",
+                        lambda steps, warmup, budget_s: real_chain(steps, warmup, 1e-9))
     monkeypatch.setattr(bench, "cpu_config1_sample", lambda budget_s=0.0: real_cfg1(0.0))
     monkeypatch.setattr("sys.argv", ["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1"])
     bench.main()
@@ -29,7 +30,9 @@ def test_reference_arm_json_line(monkeypatch, capsys):
     assert d["value"] > 0 and d["e2e"]["value"] == d["value"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
-    assert "workload" in d["config"]
+    assert d["cpu_baseline"]["steps_timed"] == d["steps"]
+    assert "first 1 of 32 layers" in d["cpu_baseline"]["sample"]
+    assert "workload" in d["config"] and "whole host CPU" in d["config"]["scope"]
 
 
 @pytest.mark.parametrize("page_size", [1, 16, 5])
