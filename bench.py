@@ -562,13 +562,18 @@ def kv_requests(seed: int):
 
 
 def _kv_caches(dev, fill_seed=None):
+    """The 32 per-layer caches [KV_NB, 2, 16, 8, 128] bf16 as views of one
+    allocation (layer stride KV_NB blocks), so the copy-engine path can move a
+    run of blocks of every layer with one 2-D copy; the kernels see the same
+    per-layer tensors either way."""
     import torch
 
-    if fill_seed is None:
-        return [torch.zeros(KV_NB, *KV_SLAB, dtype=torch.bfloat16, device=dev) for _ in range(KV_L)]
-    g = torch.Generator(device=dev).manual_seed(fill_seed)
-    return [torch.randn(KV_NB, *KV_SLAB, generator=g, device=dev).to(torch.bfloat16)
-            for _ in range(KV_L)]
+    whole = torch.zeros(KV_L, KV_NB, *KV_SLAB, dtype=torch.bfloat16, device=dev)
+    if fill_seed is not None:
+        g = torch.Generator(device=dev).manual_seed(fill_seed)
+        for layer in whole.unbind(0):
+            layer.copy_(torch.randn(KV_NB, *KV_SLAB, generator=g, device=dev))
+    return list(whole.unbind(0))
 
 
 def _time_copy(fn, steps, warmup):
@@ -654,26 +659,40 @@ def kv_host_path(sc, dc, sids, dids, steps, warmup):
             "round_trip_gbs": round(nbytes / ((ms_g + ms_s) * 1e-3) / 1e9, 2)}
 
 
-def _overlap_one(g, chain_ms, copy, nbytes, reps):
+def _overlap_one(g, chain_ms, copy, nbytes, reps, threaded=False):
     """The chain graph `g` on the current stream and `copy` on a side stream,
-    launched interleaved so both run for about the same time."""
+    launched interleaved so both run for about the same time.  threaded: the
+    copies are issued by a second host thread (the copy-engine path spends
+    milliseconds of host time per call, which must not delay the chain's
+    launches)."""
     import torch
 
     main = torch.cuda.current_stream()
     side = torch.cuda.Stream()
     with torch.cuda.stream(side):
-        copy_ms = _time_copy(copy, 10, 3)
+        copy_ms = _time_copy(copy, 10 if not threaded else 3, 3 if not threaded else 1)
     n_copy = max(1, round(reps * chain_ms / copy_ms))
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     ev[0].record(main)
     ev[2].record(side)
-    for i in range(max(reps, n_copy)):
-        if i < reps:
-            g.replay()
-        if i < n_copy:
+    if threaded:
+        def issue():
             with torch.cuda.stream(side):
-                copy()
+                for _ in range(n_copy):
+                    copy()
+        th = threading.Thread(target=issue)
+        th.start()
+        for _ in range(reps):
+            g.replay()
+        th.join()
+    else:
+        for i in range(max(reps, n_copy)):
+            if i < reps:
+                g.replay()
+            if i < n_copy:
+                with torch.cuda.stream(side):
+                    copy()
     ev[1].record(main)
     ev[3].record(side)
     torch.cuda.synchronize()
@@ -695,7 +714,7 @@ def _overlap_chain(dev, copies, nbytes, reps):
     chain_ms = time_replays(g, reps, 5) / reps
     out = {"chain_ms_alone": round(chain_ms, 4), "copy_bytes": nbytes}
     for name, copy in copies.items():
-        out[name] = _overlap_one(g, chain_ms, copy, nbytes, reps)
+        out[name] = _overlap_one(g, chain_ms, copy, nbytes, reps, threaded="copy_engine" in name)
     del g
     return out
 
@@ -817,12 +836,25 @@ def _pair_overlap(role, pair_lp, pair_hp, imported, caches, peer_caches, sids, d
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         ev[0].record(main)
         ev[2].record(side)
-        for i in range(max(reps if role == "hp" else 0, n_copy if fn is not None else 0)):
-            if role == "hp" and i < reps:
-                g.replay()
-            if fn is not None and i < n_copy:
+        if role == "hp" and fn is not None and m == 3:
+            # copy-engine copies take milliseconds of host time per call: issue
+            # them from a second thread so the chain's launches are not delayed
+            def issue(fn=fn, n=n_copy):
                 with torch.cuda.stream(side):
-                    fn()
+                    for _ in range(n):
+                        fn()
+            th = threading.Thread(target=issue)
+            th.start()
+            for _ in range(reps):
+                g.replay()
+            th.join()
+        else:
+            for i in range(max(reps if role == "hp" else 0, n_copy if fn is not None else 0)):
+                if role == "hp" and i < reps:
+                    g.replay()
+                if fn is not None and i < n_copy:
+                    with torch.cuda.stream(side):
+                        fn()
         ev[1].record(main)
         ev[3].record(side)
         torch.cuda.synchronize()
@@ -1179,19 +1211,30 @@ def run_side_workload(args, ws, rank, local):
 
         ch = build_chain(dev, seed=1)
         layers = ch["layers"][: args.layers]
-        act = pb.activation_ops
+        ln, pe, act = pb.layernorm_ops, pb.pos_encoding_ops, pb.activation_ops
+        pos, cache = ch["positions"], ch["cache"]
+        one = {
+            "silu_and_mul": (lambda b: act.silu_and_mul(b["act"], b["gate_up"]), B_SILU),
+            "fused_add_rms_norm": (lambda b: ln.fused_add_rms_norm(b["attn"], b["residual2"],
+                                                                   b["w_post"], EPS), B_FUSED),
+            "rotary_embedding": (lambda b: pe.rotary_embedding(pos, b["q"], b["k"], HD, cache,
+                                                               True), B_ROPE),
+            "rms_norm": (lambda b: ln.rms_norm(b["act"][:, :H], b["hidden"], b["w_in"], EPS),
+                         B_RMS),
+        }[args.op]
         s_ = torch.cuda.Stream()
         s_.wait_stream(torch.cuda.current_stream())
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr, stream=s_):
             for b in layers:
-                act.silu_and_mul(b["act"], b["gate_up"])
+                one[0](b)
         for _ in range(args.steps):
             gr.replay()
         torch.cuda.synchronize()
-        line = {"metric": "silu_and_mul graph replays for a graph-level ncu capture",
+        line = {"metric": f"{args.op} graph replays (T=512 Sarathi batch, Llama-3-8B shapes) "
+                          "for ncu captures",
                 "launches_per_replay": len(layers), "replays": args.steps,
-                "algorithmic_bytes_per_launch": B_SILU}
+                "algorithmic_bytes_per_launch": one[1]}
     elif args.workload == "sweep":
         line = {"metric": "per-op HBM GB/s, token sweep", "sweep": sweep(dev) if rank == 0 else None,
                 "peak_gbs": peaks()["hbm_gbs"]}
@@ -1222,9 +1265,13 @@ def main():
                     default="chain",
                     help="chain: the headline op chain (the driver's line); kv: LP->HP "
                          "promotion; sweep: per-op token sweep; moe: Mixtral-8x7B routing; "
-                         "opgraph: silu_and_mul graph replays for a graph-level ncu capture")
+                         "opgraph: one op's launches over distinct layer buffers, as a CUDA "
+                         "graph (for ncu captures)")
     ap.add_argument("--layers", type=int, default=32,
                     help="opgraph: launches (layers) per graph")
+    ap.add_argument("--op", default="silu_and_mul",
+                    choices=["silu_and_mul", "fused_add_rms_norm", "rotary_embedding", "rms_norm"],
+                    help="opgraph: the op whose launches the graph holds")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     KV_NB = args.kv_blocks

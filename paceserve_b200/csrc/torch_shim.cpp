@@ -351,10 +351,16 @@ void run_kv_copy(const std::vector<void*>& src, const std::vector<void*>& dst,
     TORCH_CHECK(s.size() == d.size(), op, ": block id lists differ in length");
     counter_ptr(bad_pairs, exec, op, "bad_pairs");  // validates the counter before any copy
     int64_t nbad = 0, issued = 0;
-    check_status(pace_kv_copy_blocks_ce(src.data(), dst.data(), (int)src.size(), s.data(),
-                                        d.data(), (int64_t)s.size(), block_bytes, src_blocks,
-                                        dst_blocks, &nbad, &issued, stream),
-                 op);
+    int rc;
+    {
+      // One copy call per run of blocks can take milliseconds of host time for
+      // fragmented tables: let other Python threads (the serving loop) run.
+      py::gil_scoped_release no_gil;
+      rc = pace_kv_copy_blocks_ce(src.data(), dst.data(), (int)src.size(), s.data(), d.data(),
+                                  (int64_t)s.size(), block_bytes, src_blocks, dst_blocks, &nbad,
+                                  &issued, stream);
+    }
+    check_status(rc, op);
     if (bad_pairs.has_value() && nbad > 0) bad_pairs->add_(nbad);  // stream-ordered, as the kernels count
     return;
   }
