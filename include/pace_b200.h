@@ -86,6 +86,30 @@ int pace_rotary_embedding(const int64_t* positions, void* query, void* key, int6
                           const void* cos_sin_cache, int cache_dtype, int rot_dim,
                           int64_t max_position, int is_neox, int dtype, cudaStream_t stream);
 
+/* ---- qkv projection with the rotary embedding in its epilogue ----------
+ * qkv_out[T, (nq + 2 nkv) * head_size] = hidden[T, hidden_size] @ weight^T on
+ * the tcgen05 tensor cores (fp32 accumulation), with heads 0 .. nq + nkv - 1
+ * (q, then k) rotated as pace_rotary_embedding does (NeoX or GPT-J pairs,
+ * cache [max_position, rot_dim] of cache_dtype F32 or dtype) before the one
+ * rounding to dtype; v heads are stored as computed.  weight is the
+ * contiguous [(nq + 2 nkv) * head_size, hidden_size] projection matrix
+ * (row-major, as torch.nn.Linear holds it).  dtype in {F16, BF16}; head_size =
+ * rot_dim = 128; hidden_size and both row strides multiples of 8 elements;
+ * qkv_out, hidden, weight and the cache 16-byte aligned.  Tokens whose
+ * position lies outside [0, max_position) are stored unrotated.
+ * fault_flags (optional device int32, may be NULL): bit 30 is OR-ed in when a
+ * bounded device wait expires (the output is then incomplete).
+ * Replaces qkv_proj followed by rotary_emb in LlamaAttention.forward
+ * (paceserve/model_executor/models/llama.py:176-178): F.linear, then
+ * rotary_embedding (csrc/pos_encoding.cpp:3-9). */
+int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
+                       const int64_t* positions, int64_t num_tokens, int64_t hidden_size,
+                       int num_heads, int num_kv_heads, int head_size,
+                       int64_t hidden_row_stride, int64_t out_row_stride,
+                       const void* cos_sin_cache, int cache_dtype, int rot_dim,
+                       int64_t max_position, int is_neox, int dtype, int32_t* fault_flags,
+                       cudaStream_t stream);
+
 /* ---- gated and element-wise activations ---------------------------------
  * *_and_mul: input [T, 2d] -> out [T, d], out = act(x[:, :d]) * x[:, d:].
  * Replaces silu_and_mul (csrc/activation.cpp:3-13,

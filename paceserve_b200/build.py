@@ -48,6 +48,7 @@ CUDA_SOURCES = [
     "moe_kernels.cu",
     "kv_transfer_kernels.cu",
     "kv_append_kernels.cu",
+    "gemm_rope_kernels.cu",
 ]
 
 

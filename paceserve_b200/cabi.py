@@ -53,6 +53,11 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _P, _P, c_int64, c_int, c_int, c_int, c_int64, c_int64, _P, c_int, c_int, c_int64,
          c_int, c_int, _P],
     ),
+    "pace_qkv_proj_rope": (
+        c_int,
+        [_P, _P, _P, _P, c_int64, c_int64, c_int, c_int, c_int, c_int64, c_int64, _P, c_int,
+         c_int, c_int64, c_int, c_int, _P, _P],
+    ),
     "pace_silu_and_mul": (c_int, _ACT),
     "pace_gelu_and_mul": (c_int, _ACT),
     "pace_gelu_tanh_and_mul": (c_int, _ACT),

@@ -179,6 +179,54 @@ void rotary_embedding(Tensor& positions, Tensor& query, Tensor& key, int64_t hea
                op);
 }
 
+// qkv = hidden @ weight^T with the rotary embedding of the q and k heads
+// applied before the output is rounded (tcgen05 GEMM + rope epilogue).  It
+// replaces qkv_proj followed by rotary_embedding
+// (paceserve/model_executor/models/llama.py:176-178); `qkv` is the [T, (nq +
+// 2 nkv) * head_size] output the split into q, k, v views reads.
+void qkv_proj_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& weight, Tensor& positions,
+                               int64_t head_size, int64_t num_heads, int64_t num_kv_heads,
+                               Tensor& cos_sin_cache, bool is_neox,
+                               const c10::optional<Tensor>& fault_flags) {
+  const char* op = "qkv_proj_rotary_embedding";
+  check_cuda(hidden, op, "hidden");
+  check_same_device(qkv, hidden, op);
+  check_same_device(weight, hidden, op);
+  check_same_device(positions, hidden, op);
+  check_same_device(cos_sin_cache, hidden, op);
+  TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 || hidden.scalar_type() == at::kHalf, op,
+              ": hidden must be bfloat16 or float16");
+  TORCH_CHECK(qkv.scalar_type() == hidden.scalar_type() &&
+                  weight.scalar_type() == hidden.scalar_type(),
+              op, ": qkv, hidden and weight must share a dtype");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && positions.is_contiguous(), op,
+              ": positions must be a contiguous int64 tensor");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(), op,
+              ": cos_sin_cache must be a contiguous [max_position, rot_dim] tensor");
+  TORCH_CHECK(num_heads >= 0 && num_kv_heads >= 0 && head_size > 0, op, ": bad head counts");
+  const Rows h = rows_of(hidden, op, "hidden");
+  TORCH_CHECK(hidden.dim() == 2, op, ": hidden must be [T, hidden_size]");
+  TORCH_CHECK(qkv.dim() == 2 && qkv.size(0) == h.rows, op, ": qkv must be [T, ",
+              (num_heads + 2 * num_kv_heads) * head_size, "]");
+  const Rows o = rows_of(qkv, op, "qkv");
+  const int64_t n = (num_heads + 2 * num_kv_heads) * head_size;
+  TORCH_CHECK(o.width == n, op, ": qkv width ", o.width, " != (num_heads + 2 * num_kv_heads) * head_size = ", n);
+  TORCH_CHECK(weight.dim() == 2 && weight.is_contiguous() && weight.size(0) == n &&
+                  weight.size(1) == h.width,
+              op, ": weight must be a contiguous [", n, ", ", h.width, "] tensor");
+  TORCH_CHECK(positions.numel() >= h.rows, op, ": positions has ", positions.numel(),
+              " entries for ", h.rows, " tokens");
+  const at::cuda::CUDAGuard guard(hidden.device());
+  int32_t* fault = counter_ptr(fault_flags, hidden.device(), op, "fault_flags");
+  check_status(pace_qkv_proj_rope(qkv.data_ptr(), hidden.data_ptr(), weight.data_ptr(),
+                                  positions.data_ptr<int64_t>(), h.rows, h.width, (int)num_heads,
+                                  (int)num_kv_heads, (int)head_size, h.stride, o.stride,
+                                  cos_sin_cache.data_ptr(), pace_dtype(cos_sin_cache),
+                                  (int)cos_sin_cache.size(1), cos_sin_cache.size(0),
+                                  is_neox ? 1 : 0, pace_dtype(hidden), fault, stream_of(hidden)),
+               op);
+}
+
 // ------------------------------------------------------------ activation --
 using ActFn = int (*)(void*, const void*, int64_t, int64_t, int64_t, int64_t, int, cudaStream_t);
 
@@ -633,6 +681,12 @@ PYBIND11_MODULE(_C, m) {
          "Apply GPT-NeoX or GPT-J style rotary embedding to query and key", py::arg("positions"),
          py::arg("query"), py::arg("key"), py::arg("head_size"), py::arg("cos_sin_cache"),
          py::arg("is_neox"));
+  pe.def("qkv_proj_rotary_embedding", &qkv_proj_rotary_embedding,
+         "qkv = hidden @ weight^T on the tensor cores with the rotary embedding applied to the "
+         "q and k heads before rounding (fused qkv_proj + rotary_embedding).",
+         py::arg("qkv"), py::arg("hidden"), py::arg("weight"), py::arg("positions"),
+         py::arg("head_size"), py::arg("num_heads"), py::arg("num_kv_heads"),
+         py::arg("cos_sin_cache"), py::arg("is_neox"), py::arg("fault_flags") = py::none());
 
   auto act = m.def_submodule("activation_ops");
   act.def("silu_and_mul", &silu_and_mul, "Activation function used in SwiGLU.", py::arg("out"),

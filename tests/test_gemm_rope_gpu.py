@@ -1,0 +1,189 @@
+"""GPU parity of the fused qkv projection + rotary embedding (tcgen05 GEMM with
+the rotation in its epilogue) against the fp32 oracle: the GEMM of the same
+bf16/fp16 inputs in fp32, then the oracle's rotation.  Tolerance: the float
+rule of the per-layer ops, max|got - ref| / max|ref| <= 1e-2, plus a per-element
+bound of a few storage-type ulps (the only differences are the fp32 summation
+order and the one final rounding)."""
+import ctypes
+
+import pytest
+import torch
+
+from oracle import ops_ref
+from paceserve_b200 import cabi, pos_encoding_ops
+from tests._util import REL_TOL, rel_err
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _gen(seed):
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    return g
+
+
+def reference(hidden, weight, positions, nq, nkv, hd, cache, neox):
+    """fp32 oracle: qkv = hidden @ weight^T from the same 16-bit inputs, then
+    the q and k heads rotated by ops_ref.rotary_embedding_fp32."""
+    qkv = hidden.float() @ weight.float().t()
+    q, k = ops_ref.rotary_embedding_fp32(positions, qkv[:, : nq * hd],
+                                         qkv[:, nq * hd: (nq + nkv) * hd], hd, cache, neox)
+    return torch.cat([q, k, qkv[:, (nq + nkv) * hd:]], dim=1)
+
+
+def make_case(T, H, nq, nkv, dtype, seed, max_pos=8192, pos_hi=None):
+    g = _gen(seed)
+    hd = 128
+    hidden = torch.randn(T, H, generator=g).to(dtype)
+    # weights scaled like a trained projection so outputs stay O(1)
+    weight = (torch.randn((nq + 2 * nkv) * hd, H, generator=g) / H ** 0.5).to(dtype)
+    positions = torch.randint(0, pos_hi or max_pos, (T,), generator=g)
+    cache = ops_ref.cos_sin_cache(hd, max_pos, 500000.0)
+    return hidden, weight, positions, cache
+
+
+def check(got, ref, dtype, tight=True):
+    assert rel_err(got, ref) <= REL_TOL
+    if tight:
+        # one rounding of the fp32 accumulator: within one storage ulp of each
+        # element, plus 0.1 % of the largest magnitude for the summation order
+        g, r = got.float().cpu(), ref.float().cpu()
+        bound = torch.finfo(dtype).eps * r.abs() + 1e-3 * r.abs().max()
+        assert ((g - r).abs() <= bound).all(), ((g - r).abs() - bound).max().item()
+
+
+@pytest.mark.parametrize("T", [1, 17, 128, 300, 512])
+@pytest.mark.parametrize("neox", [True, False])
+def test_llama3_8b_shape(T, neox):
+    nq, nkv, hd, H = 32, 8, 128, 4096
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, T)
+    qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
+    fault = torch.zeros(1, dtype=torch.int32, device=DEV)
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden.to(DEV), weight.to(DEV),
+                                               positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                               neox, fault)
+    torch.cuda.synchronize()
+    assert fault.item() == 0
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, neox), torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("cache_16bit", [False, True])
+def test_dtypes_and_cache_types(dtype, cache_16bit):
+    T, H, nq, nkv, hd = 130, 1024, 4, 2, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, dtype, 5)
+    if cache_16bit:
+        cache = cache.to(dtype)
+    qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=dtype, device=DEV)
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden.to(DEV), weight.to(DEV),
+                                               positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                               True)
+    torch.cuda.synchronize()
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache.float(), True), dtype)
+
+
+@pytest.mark.parametrize("H", [64, 200, 4104])
+def test_hidden_not_a_multiple_of_the_k_block(H):
+    # the K tail past the last full 64-element block is zero-filled by TMA
+    T, nq, nkv, hd = 40, 2, 1, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, H)
+    qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden.to(DEV), weight.to(DEV),
+                                               positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                               True)
+    torch.cuda.synchronize()
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
+
+
+def test_strided_rows_and_out_of_range_positions():
+    T, H, nq, nkv, hd = 200, 512, 4, 2, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, 9)
+    positions[::7] = -3
+    positions[3::11] = 8192  # == max_position: out of range
+    big = torch.zeros(T, H + 64, dtype=torch.bfloat16)
+    big[:, :H] = hidden
+    n = (nq + 2 * nkv) * hd
+    out_big = torch.full((T, n + 256), 7.0, dtype=torch.bfloat16, device=DEV)
+    qkv = out_big[:, :n]
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, big.to(DEV)[:, :H], weight.to(DEV),
+                                               positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                               True)
+    torch.cuda.synchronize()
+    ref = reference(hidden, weight, positions, nq, nkv, hd, cache, True)
+    check(qkv, ref, torch.bfloat16)
+    # tokens out of range are the plain projection
+    plain = hidden.float() @ weight.float().t()
+    bad = (positions < 0) | (positions >= 8192)
+    check(qkv.cpu()[bad], plain[bad], torch.bfloat16)
+    # the padding columns past the output row are untouched
+    assert (out_big[:, n:].cpu() == 7.0).all()
+
+
+def test_matches_unfused_projection_then_rope():
+    """The fused result against the path it replaces: a library GEMM, then the
+    rotary_embedding op on the q/k views.  The unfused path rounds twice, so the
+    two differ by at most a couple of bf16 ulps."""
+    T, H, nq, nkv, hd = 512, 4096, 32, 8, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, 21)
+    hd_, wd, pd, cd = hidden.to(DEV), weight.to(DEV), positions.to(DEV), cache.to(DEV)
+    unfused = hd_ @ wd.t()
+    pos_encoding_ops.rotary_embedding(pd, unfused[:, : nq * hd], unfused[:, nq * hd: (nq + nkv) * hd],
+                                      hd, cd, True)
+    fused = torch.empty_like(unfused)
+    pos_encoding_ops.qkv_proj_rotary_embedding(fused, hd_, wd, pd, hd, nq, nkv, cd, True)
+    torch.cuda.synchronize()
+    ref = reference(hidden, weight, positions, nq, nkv, hd, cache, True)
+    check(fused, ref, torch.bfloat16)
+    check(unfused, ref, torch.bfloat16, tight=False)
+
+
+def test_graph_capture_and_repeat():
+    T, H, nq, nkv, hd = 256, 2048, 8, 2, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, 4)
+    hd_, wd, pd, cd = hidden.to(DEV), weight.to(DEV), positions.to(DEV), cache.to(DEV)
+    qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hd_, wd, pd, hd, nq, nkv, cd, True)
+    torch.cuda.current_stream().wait_stream(s)
+    first = qkv.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hd_, wd, pd, hd, nq, nkv, cd, True)
+    qkv.zero_()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(qkv, first)  # deterministic: same bits every run
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
+
+
+def test_c_abi_direct_call():
+    lib = cabi.load()
+    T, H, nq, nkv, hd = 64, 256, 2, 1, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, 2)
+    hd_, wd, pd, cd = hidden.to(DEV), weight.to(DEV), positions.to(DEV), cache.to(DEV)
+    n = (nq + 2 * nkv) * hd
+    out = torch.empty(T, n, dtype=torch.bfloat16, device=DEV)
+    st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(), T, H,
+                                nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd, 8192, 1,
+                                cabi.PACE_BF16, None, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == cabi.PACE_OK, lib.pace_last_error()
+    torch.cuda.synchronize()
+    check(out, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
+
+
+def test_rejected_shapes():
+    T, H, nq, nkv = 4, 256, 2, 1
+    hidden = torch.randn(T, H, device=DEV).bfloat16()
+    cache = torch.randn(8192, 64, device=DEV)
+    weight = torch.randn((nq + 2 * nkv) * 64, H, device=DEV).bfloat16()
+    qkv = torch.empty(T, (nq + 2 * nkv) * 64, dtype=torch.bfloat16, device=DEV)
+    pos = torch.zeros(T, dtype=torch.long, device=DEV)
+    with pytest.raises(RuntimeError, match="head_size"):
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden, weight, pos, 64, nq, nkv, cache, True)
+    with pytest.raises(RuntimeError, match="bfloat16 or float16"):
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv.float(), hidden.float(), weight.float(), pos,
+                                                   64, nq, nkv, cache, True)
