@@ -45,6 +45,7 @@ T = T_PREFILL + T_DECODE
 H, I, NQ, NKV, HD, L = 4096, 14336, 32, 8, 128, 32
 MAX_POS, THETA, EPS = 8192, 500000.0, 1e-5
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 NOMINAL_HBM_GBS = 7700.0  # B200 HGX HBM3e figure; the roofline uses the measured copy peak
 
 # Algorithmic bytes (bf16 activations, fp32 cos/sin cache), per launch at T tokens
@@ -68,9 +69,11 @@ def peaks() -> dict:
     try:
         with open(path) as f:
             p = json.load(f)
-        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "source": "measured"}
     except Exception:
-        return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
+        return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+                "source": "fallback"}
 
 
 def ncu_traffic(kernel_key: str):
@@ -1146,6 +1149,70 @@ def moe_routing(dev, reps=50):
     return out
 
 
+def qkv_rope_bench(dev, tokens=(1, 128, 512, 2048), reps=10):
+    """The fused qkv projection + rotary embedding (tcgen05 GEMM, rope in the
+    epilogue) against the path it replaces: cuBLAS (torch.matmul) for the
+    projection, then the rotary_embedding op on the q/k views.  Llama-3-8B
+    (hidden 4096 -> 6144 = 32 q + 8 k + 8 v heads of 128), bf16, fp32 cache,
+    positions as the Sarathi batch draws them.  Each variant is a CUDA graph
+    over 4 distinct weight matrices (4 x 50 MB > L2); the fused output is
+    checked against the unfused one within the bf16 rule."""
+    import torch
+
+    import paceserve_b200 as pb
+
+    nq, nkv = NQ, NKV
+    n = (nq + 2 * nkv) * HD
+    nbuf = 4
+    g_ = torch.Generator(device=dev).manual_seed(77)
+    weights = [(torch.randn(n, H, generator=g_, device=dev) / H ** 0.5).bfloat16()
+               for _ in range(nbuf)]
+    cache = rope_cache(dev)
+    peak = peaks()
+    rows = []
+    for t in tokens:
+        xs = [torch.randn(t, H, generator=g_, device=dev).bfloat16() for _ in range(nbuf)]
+        pos = torch.randint(0, MAX_POS, (t,), generator=g_, device=dev)
+        outs = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        refs = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+
+        def fused():
+            for x, w, o in zip(xs, weights, outs):
+                pb.pos_encoding_ops.qkv_proj_rotary_embedding(o, x, w, pos, HD, nq, nkv, cache,
+                                                              True)
+
+        def gemm():
+            for x, w, o in zip(xs, weights, refs):
+                torch.matmul(x, w.t(), out=o)
+
+        def unfused():
+            for x, w, o in zip(xs, weights, refs):
+                torch.matmul(x, w.t(), out=o)
+                pb.pos_encoding_ops.rotary_embedding(pos, o[:, : nq * HD],
+                                                     o[:, nq * HD: (nq + nkv) * HD], HD, cache,
+                                                     True)
+
+        res = {"T": t}
+        for name, fn in (("fused_us", fused), ("cublas_gemm_us", gemm),
+                         ("cublas_gemm_plus_rope_us", unfused)):
+            fn()  # eager once (the shim's workspace is allocated outside capture)
+            gr = capture(fn)
+            res[name] = round(time_replays(gr, reps, 3) * 1e3 / (reps * nbuf), 3)
+            del gr
+        torch.cuda.synchronize()
+        ref = refs[-1].float()
+        err = ((outs[-1].float() - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()
+        flops = 2.0 * t * n * H
+        res["tflops"] = round(flops / (res["fused_us"] * 1e-6) / 1e12, 1)
+        res["frac_of_bf16_peak"] = round(res["tflops"] / peak["bf16_tflops"], 4)
+        res["speedup_vs_unfused"] = round(res["cublas_gemm_plus_rope_us"] / res["fused_us"], 3)
+        res["rel_err_vs_unfused"] = round(err, 5)
+        rows.append(res)
+        del xs, outs, refs
+        torch.cuda.empty_cache()
+    return rows
+
+
 # ------------------------------------------------------------------ main --
 def init_dist():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1355,6 +1422,11 @@ def main():
         line["moe"] = {"what": "BASELINE config 4: Mixtral-8x7B routing, topk_softmax (E=8, top-2, "
                                "renormalised) + moe_align_block_size (block 64); latency bound",
                        "rows": moe_routing(dev, reps=50)}
+        torch.cuda.empty_cache()
+        line["qkv_rope"] = {"what": "fused qkv projection + rotary embedding (tcgen05 GEMM, rope in "
+                                    "the epilogue) vs cuBLAS GEMM then the rope op; Llama-3-8B "
+                                    "4096 -> 6144, bf16, 4 weight buffers per graph (> L2)",
+                            "peak_tflops": pk["bf16_tflops"], "rows": qkv_rope_bench(dev)}
     if ws > 1:
         del ch
         torch.cuda.empty_cache()

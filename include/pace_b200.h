@@ -16,6 +16,7 @@
 #ifndef PACE_B200_H_
 #define PACE_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 #include <cuda_runtime_api.h>
 
@@ -97,18 +98,27 @@ int pace_rotary_embedding(const int64_t* positions, void* query, void* key, int6
  * rot_dim = 128; hidden_size and both row strides multiples of 8 elements;
  * qkv_out, hidden, weight and the cache 16-byte aligned.  Tokens whose
  * position lies outside [0, max_position) are stored unrotated.
+ * workspace: device memory of at least pace_qkv_proj_rope_workspace_size()
+ * bytes (for this shape and device), 256-byte aligned, ZERO-FILLED before its
+ * first use; every call leaves it valid for the next (its tile counters back
+ * at zero, at an offset that does not depend on the shape), so one zeroed
+ * workspace serves any number of stream-ordered calls of any shapes that fit
+ * in it.  Calls that may run concurrently need separate workspaces.
  * fault_flags (optional device int32, may be NULL): bit 30 is OR-ed in when a
- * bounded device wait expires (the output is then incomplete).
+ * bounded device wait expires (the output is then incomplete and the
+ * workspace must be zero-filled again before reuse).
  * Replaces qkv_proj followed by rotary_emb in LlamaAttention.forward
  * (paceserve/model_executor/models/llama.py:176-178): F.linear, then
  * rotary_embedding (csrc/pos_encoding.cpp:3-9). */
+size_t pace_qkv_proj_rope_workspace_size(int64_t num_tokens, int64_t hidden_size, int num_heads,
+                                         int num_kv_heads, int device);
 int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
                        const int64_t* positions, int64_t num_tokens, int64_t hidden_size,
                        int num_heads, int num_kv_heads, int head_size,
                        int64_t hidden_row_stride, int64_t out_row_stride,
                        const void* cos_sin_cache, int cache_dtype, int rot_dim,
-                       int64_t max_position, int is_neox, int dtype, int32_t* fault_flags,
-                       cudaStream_t stream);
+                       int64_t max_position, int is_neox, int dtype, void* workspace,
+                       size_t workspace_bytes, int32_t* fault_flags, cudaStream_t stream);
 
 /* ---- gated and element-wise activations ---------------------------------
  * *_and_mul: input [T, 2d] -> out [T, d], out = act(x[:, :d]) * x[:, d:].

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_uint64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
 
 LIBRARY_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libpace_b200.so")
 
@@ -56,8 +56,9 @@ SIGNATURES: dict[str, tuple] = {
     "pace_qkv_proj_rope": (
         c_int,
         [_P, _P, _P, _P, c_int64, c_int64, c_int, c_int, c_int, c_int64, c_int64, _P, c_int,
-         c_int, c_int64, c_int, c_int, _P, _P],
+         c_int, c_int64, c_int, c_int, _P, c_size_t, _P, _P],
     ),
+    "pace_qkv_proj_rope_workspace_size": (c_size_t, [c_int64, c_int64, c_int, c_int, c_int]),
     "pace_silu_and_mul": (c_int, _ACT),
     "pace_gelu_and_mul": (c_int, _ACT),
     "pace_gelu_tanh_and_mul": (c_int, _ACT),

@@ -10,71 +10,98 @@
 // rounds the GEMM output, then rotates and rounds again) and the separate rope
 // launch and its 4(nq+nkv)hd bytes per token of HBM traffic disappear.
 //
-// Tiling: one 128 x 128 output tile per CTA, 128 columns = one head, so both
-// halves of every NeoX pair (i, i + 64) and every GPT-J pair (2i, 2i + 1) sit
-// in the same tile.  K is consumed in 64-element (128-byte) blocks through a
-// 4-stage shared-memory ring filled by TMA (128-byte swizzle, no multicast).
-// Warp roles: warps 0-3 run the epilogue (warp w owns TMEM lanes 32w..32w+31,
-// i.e. tile rows), warp 4 issues the TMA loads, warp 5 issues tcgen05.mma
-// (M=128, N=128, K=16, fp32 accumulator in 128 TMEM columns) and commits each
-// stage back to the producer.  Every mbarrier wait is bounded by %globaltimer;
-// on expiry the CTA records bit 30 in the caller's fault word, stops issuing,
-// waits (bounded again) for its own copies and MMAs, frees TMEM and returns.
+// Work decomposition (stream-K): the output is cut into 128 x 256 tiles (two
+// heads, so both halves of every NeoX pair (i, i + 64) and every GPT-J pair
+// (2i, 2i + 1) of a head sit in one tile), each tile into 64-element K blocks,
+// and the (tile, K block) units are split evenly over one persistent CTA per
+// SM.  A CTA whose range covers a whole tile finishes it directly; a tile
+// shared by several CTAs is finished by the CTA that contributes last: every
+// contributor stores its fp32 partial sum in the caller's workspace and counts
+// itself in the tile's counter, and the one that completes the count adds the
+// partials in segment order (so the result does not depend on which CTA came
+// last), rotates and stores.  No CTA ever waits for another.  At T=512 this
+// gives every SM 41.5 units instead of one or two whole tiles.
+//
+// Inside a CTA: a 4-stage shared-memory ring of A (128 x 64) and B (256 x 64)
+// blocks filled by TMA (128-byte swizzle, no multicast; warp 4), tcgen05.mma
+// (M=128, N=256, K=16, fp32) issued by one thread of warp 5 into one of two
+// 256-column TMEM accumulators, and 4 epilogue warps (warp w owns TMEM lanes
+// 32w..32w+31, i.e. tile rows) that drain one accumulator while the MMAs fill
+// the other.  Every mbarrier wait is bounded by %globaltimer; on expiry the
+// CTA records bit 30 in the caller's fault word, stops issuing, waits (bounded
+// again) for its own copies and MMAs, frees TMEM and returns.
 #include "tcgen05.cuh"
 
 namespace pace {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64;
+constexpr int BM = 128, BN = 256, BK = 64, HEAD = 128;
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter: one per head of the tile
 constexpr int THREADS = (EPI_WARPS + 2) * 32;
+constexpr int TMEM_COLS = 2 * BN;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int SLOT_FLOATS = BM * BN;  // one partial tile
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
 constexpr int32_t kFaultTimeout = 1 << 30;
+constexpr int kEpiBarrier = 1;  // named barrier of the 256 epilogue threads
 
 struct Ctl {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t accum;
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
   uint64_t drain;
   uint32_t tmem;
   int abort;
+  int last;  // epilogue: this CTA completes the current shared tile
 };
 static_assert(sizeof(Ctl) <= 256, "");
+
+// Static split of the (tile, K block) units over the persistent CTAs.
+struct Split {
+  int64_t units;  // tiles * k_blocks
+  int ctas;
+  int k_blocks;
+  __device__ __forceinline__ int64_t start(int c) const { return (int64_t)c * units / ctas; }
+  // the CTA whose range contains unit u
+  __device__ __forceinline__ int owner(int64_t u) const {
+    return (int)(((u + 1) * ctas - 1) / units);
+  }
+};
 
 __device__ __forceinline__ void raise_fault(Ctl* ctl, int32_t* fault) {
   *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
   if (fault) atomicOr(fault, kFaultTimeout);
 }
 
-// 16 cache entries starting at p (16-byte aligned) as floats.
-template <typename C>
-__device__ __forceinline__ void load16(const C* p, float* out) {
-  if constexpr (sizeof(C) == 4) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(p) + i);
-      out[4 * i] = v.x;
-      out[4 * i + 1] = v.y;
-      out[4 * i + 2] = v.z;
-      out[4 * i + 3] = v.w;
-    }
-  } else {
-    Traits<C>::unpack(__ldg(reinterpret_cast<const uint4*>(p)), out);
-    Traits<C>::unpack(__ldg(reinterpret_cast<const uint4*>(p) + 1), out + 8);
-  }
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kEpiBarrier), "n"(EPI_WARPS * 32) : "memory");
+}
+// Barrier of the epilogue threads that also ANDs `pred` over them, so every
+// epilogue warp takes the same branch.
+__device__ __forceinline__ bool epi_all(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "n"(kEpiBarrier), "n"(EPI_WARPS * 32)
+      : "memory");
+  return r != 0;
 }
 
-// 8 cache entries starting at p (16-byte aligned) as floats.
-template <typename C>
-__device__ __forceinline__ void load8(const C* p, float* out) {
+// n cache entries (n = 8 or 16) starting at p (16-byte aligned) as floats.
+template <typename C, int N>
+__device__ __forceinline__ void load_cs(const C* p, float* out) {
   if constexpr (sizeof(C) == 4) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < N / 4; ++i) {
       const float4 v = __ldg(reinterpret_cast<const float4*>(p) + i);
       out[4 * i] = v.x;
       out[4 * i + 1] = v.y;
@@ -82,7 +109,9 @@ __device__ __forceinline__ void load8(const C* p, float* out) {
       out[4 * i + 3] = v.w;
     }
   } else {
-    Traits<C>::unpack(__ldg(reinterpret_cast<const uint4*>(p)), out);
+#pragma unroll
+    for (int i = 0; i < N / 8; ++i)
+      Traits<C>::unpack(__ldg(reinterpret_cast<const uint4*>(p) + i), out + 8 * i);
   }
 }
 
@@ -92,28 +121,199 @@ __device__ __forceinline__ void store16(T* p, const float* v) {
   st_v4(p + 8, Traits<T>::pack(v + 8));
 }
 
-template <int N>
-__device__ __forceinline__ void as_float(const uint32_t (&r)[N], float* f) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) f[i] = __uint_as_float(r[i]);
+// Partials go through L2 only (.cg): the CTA that reads them back runs on
+// another SM, whose L1 may hold stale lines of the same slot from an earlier
+// call.
+__device__ __forceinline__ void st_cg_f4(float* p, float a, float b, float c, float d) {
+  __stcg(reinterpret_cast<float4*>(p), make_float4(a, b, c, d));
+}
+__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
+  return __ldcg(reinterpret_cast<const float4*>(p));
 }
 
-// grid (m tiles, heads): m fastest, so the CTAs resident together share
-// weight tiles through L2 and every weight byte is fetched from HBM once.
+// Partial-tile layout in the workspace: [16-column chunk][quarter q][row][4
+// floats], so one warp instruction (32 rows, the same chunk and quarter) reads
+// or writes 512 contiguous bytes.
+__device__ __forceinline__ float* slot_q(float* slot, int chunk, int q, int row) {
+  return slot + ((int64_t)(chunk * 4 + q) * BM + row) * 4;
+}
+
+// ---- epilogue ------------------------------------------------------------
+// A thread finishes 16-column pieces of one tile row of one head:
+//   NeoX : step i (0..3) holds x = head cols [16i, 16i+16) and
+//          y = [64+16i, 64+16i+16), rotated with cache entries 16i .. 16i+15;
+//   GPT-J: step i holds a = head cols [32i, 32i+16) and b = [32i+16, 32i+32),
+//          pairs (2p, 2p+1) rotated with cache entries 16i + p.
+// cs: the token's cache row, or null when the head is not rotated (v heads,
+// rows past the end, positions outside the cache).
+template <bool NEOX>
+__device__ __forceinline__ int col_a(int i) { return NEOX ? 16 * i : 32 * i; }
+template <bool NEOX>
+__device__ __forceinline__ int col_b(int i) { return NEOX ? 64 + 16 * i : 32 * i + 16; }
+
+template <typename C>
+__device__ __forceinline__ void load_step_cs(const C* cs, int i, float* cv, float* sv) {
+  load_cs<C, 16>(cs + 16 * i, cv);
+  load_cs<C, 16>(cs + HEAD / 2 + 16 * i, sv);
+}
+
+template <bool NEOX>
+__device__ __forceinline__ void rotate(float* a, float* b, const float* cv, const float* sv) {
+  if (NEOX) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float x = a[e], y = b[e];
+      a[e] = x * cv[e] - y * sv[e];
+      b[e] = y * cv[e] + x * sv[e];
+    }
+  } else {
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const float x0 = a[2 * p], y0 = a[2 * p + 1];
+      a[2 * p] = x0 * cv[p] - y0 * sv[p];
+      a[2 * p + 1] = y0 * cv[p] + x0 * sv[p];
+      const float x1 = b[2 * p], y1 = b[2 * p + 1];
+      b[2 * p] = x1 * cv[8 + p] - y1 * sv[8 + p];
+      b[2 * p + 1] = y1 * cv[8 + p] + x1 * sv[8 + p];
+    }
+  }
+}
+
+// Cache row of the token in row m for a head, or null (see above).
+template <typename C>
+__device__ __forceinline__ const C* cache_row(const C* cache, const int64_t* positions,
+                                              int64_t max_position, int m, bool valid,
+                                              bool rotated_head) {
+  if (!valid || !rotated_head) return nullptr;
+  const int64_t pos = positions[m];
+  return pos >= 0 && pos < max_position ? cache + pos * HEAD : nullptr;
+}
+
+// A whole tile from TMEM: this thread's row, one head (128 columns at TMEM
+// address `taddr`).  All lanes of the warp call it (TMEM loads are
+// warp-wide); `store` is false for rows past the end and absent heads.  Each
+// step's cos/sin loads are issued before its TMEM loads, so the two overlap.
+template <typename T, typename C, bool NEOX>
+__device__ __forceinline__ void finish_head_tmem(uint32_t taddr, T* o, const C* cs, bool store) {
+#pragma unroll 1
+  for (int i = 0; i < 4; ++i) {
+    float cv[16], sv[16];
+    if (cs) load_step_cs(cs, i, cv, sv);
+    uint32_t ra[16], rb[16];
+    tc::tmem_ld16(taddr + col_a<NEOX>(i), ra);
+    tc::tmem_ld16(taddr + col_b<NEOX>(i), rb);
+    tc::tmem_wait_ld(ra);
+    tc::tmem_wait_ld(rb);
+    float a[16], b[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      a[e] = __uint_as_float(ra[e]);
+      b[e] = __uint_as_float(rb[e]);
+    }
+    if (cs) rotate<NEOX>(a, b, cv, sv);
+    if (store) {
+      store16(o + col_a<NEOX>(i), a);
+      store16(o + col_b<NEOX>(i), b);
+    }
+  }
+}
+
+// This thread's row and head of a shared tile, as a partial sum: TMEM ->
+// workspace slot (chunk = head * 8 + j for the head's 16-column chunk j).
+__device__ __forceinline__ void store_partial(uint32_t taddr, float* slot, int head_in_tile,
+                                              int row, bool valid) {
+#pragma unroll 1
+  for (int j = 0; j < HEAD / 16; j += 2) {
+    uint32_t ra[16], rb[16];
+    tc::tmem_ld16(taddr + 16 * j, ra);
+    tc::tmem_ld16(taddr + 16 * j + 16, rb);
+    tc::tmem_wait_ld(ra);
+    tc::tmem_wait_ld(rb);
+    if (valid) {
+      const int ca = head_in_tile * 8 + j, cb = ca + 1;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        st_cg_f4(slot_q(slot, ca, q, row), __uint_as_float(ra[4 * q]),
+                 __uint_as_float(ra[4 * q + 1]), __uint_as_float(ra[4 * q + 2]),
+                 __uint_as_float(ra[4 * q + 3]));
+        st_cg_f4(slot_q(slot, cb, q, row), __uint_as_float(rb[4 * q]),
+                 __uint_as_float(rb[4 * q + 1]), __uint_as_float(rb[4 * q + 2]),
+                 __uint_as_float(rb[4 * q + 3]));
+      }
+    }
+  }
+}
+
+// v[0..16) += the 16 floats of (chunk, row) in a partial slot.
+__device__ __forceinline__ void add16(float* v, const float* slot, int chunk, int row) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 f = ld_cg_f4(slot_q(const_cast<float*>(slot), chunk, q, row));
+    v[4 * q] += f.x;
+    v[4 * q + 1] += f.y;
+    v[4 * q + 2] += f.z;
+    v[4 * q + 3] += f.w;
+  }
+}
+
+// Completion of a shared tile by the CTA that contributed last.  The 8
+// epilogue warps split it by column: warp w takes step w % 4 of head w / 4
+// for every valid row (lane + 32 p), so each load of a warp reads 32
+// consecutive rows of one chunk.  Partials are added in segment order.
+template <typename T, typename C, bool NEOX>
+__device__ __forceinline__ void fixup_tile(const float* slots, const Split& sp, int64_t tile_u0,
+                                           int c0, int c1, T* out_tile, int64_t out_stride,
+                                           const C* cache, const int64_t* positions,
+                                           int64_t max_position, int m0, int valid_rows,
+                                           int head0, int rot_heads, int total_heads, int warp,
+                                           int lane) {
+  const int hh = warp / 4, i = warp % 4;
+  const int head = head0 + hh;
+  if (head >= total_heads) return;
+  const bool rotated = head < rot_heads;
+  const int ca = hh * 8 + col_a<NEOX>(i) / 16, cb = hh * 8 + col_b<NEOX>(i) / 16;
+  for (int r = lane; r < valid_rows; r += 32) {
+    const C* cs = cache_row(cache, positions, max_position, m0 + r, true, rotated);
+    float a[16], b[16], cv[16], sv[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
+    if (cs) load_step_cs(cs, i, cv, sv);
+#pragma unroll 2
+    for (int c = c0; c <= c1; ++c) {
+      const int slot = sp.start(c) >= tile_u0 ? 2 * c : 2 * c + 1;
+      const float* s = slots + (int64_t)slot * SLOT_FLOATS;
+      add16(a, s, ca, r);
+      add16(b, s, cb, r);
+    }
+    if (cs) rotate<NEOX>(a, b, cv, sv);
+    T* o = out_tile + (int64_t)r * out_stride + hh * HEAD;
+    store16(o + col_a<NEOX>(i), a);
+    store16(o + col_b<NEOX>(i), b);
+  }
+}
+
+// One persistent CTA per SM (grid = min(SMs, units)); see the file comment.
+// slots: 2 partial tiles of BM x BN floats per CTA; counters: one int32 per
+// tile, zero before the call and left zero by it.
 template <typename T, typename C, bool NEOX>
 __global__ void __launch_bounds__(THREADS, 1)
     qkv_rope_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     T* __restrict__ out, int64_t out_stride, const int64_t* __restrict__ positions,
                     const C* __restrict__ cache, int64_t max_position, int num_tokens,
-                    int rot_heads, int k_blocks, int32_t* fault) {
+                    int m_tiles, int k_blocks, int rot_heads, int total_heads,
+                    int* __restrict__ counters, float* __restrict__ slots, int32_t* fault) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   Ctl* ctl = reinterpret_cast<Ctl*>(tiles + STAGES * STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM;
-  const int head = blockIdx.y;
-  const int n0 = head * BN;
+  const int cta = blockIdx.x;
+  const int n_tiles = (total_heads * HEAD + BN - 1) / BN;
+  Split sp;
+  sp.units = (int64_t)m_tiles * n_tiles * k_blocks;
+  sp.ctas = gridDim.x;
+  sp.k_blocks = k_blocks;
+  const int64_t u_begin = sp.start(cta), u_end = sp.start(cta + 1);
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
@@ -121,7 +321,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::mbar_init(&ctl->full[s], 1);
       tc::mbar_init(&ctl->empty[s], 1);
     }
-    tc::mbar_init(&ctl->accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&ctl->tmem_full[b], 1);
+      tc::mbar_init(&ctl->tmem_empty[b], EPI_WARPS);
+    }
     tc::mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     tc::fence_barrier_init();
@@ -130,147 +333,166 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc::tma_prefetch_desc(&tm_a);
     tc::tma_prefetch_desc(&tm_b);
   }
-  if (warp == 0) tc::tmem_alloc(&ctl->tmem, BN);
+  if (warp == 0) tc::tmem_alloc(&ctl->tmem, TMEM_COLS);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = ctl->tmem;
-  // hidden states and positions may be written by the previous kernel
+  // hidden states, positions and the workspace may be in use by the previous
+  // kernel of the stream
   pdl_wait();
 
   if (warp == EPI_WARPS) {
-    // ---- TMA producer --------------------------------------------------
+    // ---- TMA producer: every K block of every segment, in order ---------
     if (lane == 0) {
-      int issued = 0;
+      int64_t i = 0;
       bool ok = true;
-      for (int kb = 0; kb < k_blocks; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t use = (uint32_t)(kb / STAGES);
-        if (use > 0 && !tc::mbar_wait(&ctl->empty[s], (use - 1) & 1u, kWaitLimitNs, &ctl->abort)) {
-          ok = false;
-          break;
+      for (int64_t u = u_begin; u < u_end && ok;) {
+        const int64_t t = u / k_blocks;
+        const int kb0 = (int)(u - t * k_blocks);
+        const int kb1 = (int)min((int64_t)k_blocks, kb0 + (u_end - u));
+        const int m0 = (int)(t % m_tiles) * BM, n0 = (int)(t / m_tiles) * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++i) {
+          const int s = (int)(i % STAGES);
+          const uint32_t use = (uint32_t)(i / STAGES);
+          if (use > 0 &&
+              !tc::mbar_wait(&ctl->empty[s], (use - 1) & 1u, kWaitLimitNs, &ctl->abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = tiles + s * STAGE_BYTES;
+          tc::mbar_arrive_expect_tx(&ctl->full[s], STAGE_BYTES);
+          tc::tma_load_2d(a, &tm_a, kb * BK, m0, &ctl->full[s]);
+          tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
         }
-        uint8_t* a = tiles + s * STAGE_BYTES;
-        tc::mbar_arrive_expect_tx(&ctl->full[s], STAGE_BYTES);
-        tc::tma_load_2d(a, &tm_a, kb * BK, m0, &ctl->full[s]);
-        tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
-        issued = kb + 1;
+        u += kb1 - kb0;
       }
-      if (!ok) {
-        raise_fault(ctl, fault);
-        // let every copy already issued land before the CTA's memory is released
-        for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; ++kb)
-          tc::mbar_wait(&ctl->full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u, kWaitLimitNs,
-                        nullptr);
-      }
+      if (!ok) raise_fault(ctl, fault);
+      // every copy issued has landed before the CTA's shared memory is released
+      // (immediate when the MMAs consumed them all)
+      for (int64_t q = i > STAGES ? i - STAGES : 0; q < i; ++q)
+        tc::mbar_wait(&ctl->full[q % STAGES], (uint32_t)(q / STAGES) & 1u, kWaitLimitNs,
+                      nullptr);
     }
   } else if (warp == EPI_WARPS + 1) {
     // ---- MMA issuer ----------------------------------------------------
     if (lane == 0) {
-      constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
       constexpr uint32_t idesc = tc::umma_idesc_f16(kBf16, BM, BN);
+      int64_t i = 0;
+      int j = 0;
       bool ok = true;
-      for (int kb = 0; kb < k_blocks; ++kb) {
-        const int s = kb % STAGES;
-        if (!tc::mbar_wait(&ctl->full[s], (uint32_t)(kb / STAGES) & 1u, kWaitLimitNs,
-                           &ctl->abort)) {
+      for (int64_t u = u_begin; u < u_end && ok; ++j) {
+        const int64_t t = u / k_blocks;
+        const int kb0 = (int)(u - t * k_blocks);
+        const int kb1 = (int)min((int64_t)k_blocks, kb0 + (u_end - u));
+        const int b = j & 1;
+        const uint32_t use_b = (uint32_t)(j >> 1);
+        if (use_b > 0 &&
+            !tc::mbar_wait(&ctl->tmem_empty[b], (use_b - 1) & 1u, kWaitLimitNs, &ctl->abort)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        const uint32_t a_addr = tc::smem_u32(tiles + s * STAGE_BYTES);
-        const uint64_t ad = tc::umma_desc_sw128(a_addr);
-        const uint64_t bd = tc::umma_desc_sw128(a_addr + A_BYTES);
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int kb = kb0; kb < kb1; ++kb, ++i) {
+          const int s = (int)(i % STAGES);
+          if (!tc::mbar_wait(&ctl->full[s], (uint32_t)(i / STAGES) & 1u, kWaitLimitNs,
+                             &ctl->abort)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a_addr = tc::smem_u32(tiles + s * STAGE_BYTES);
+          const uint64_t ad = tc::umma_desc_sw128(a_addr);
+          const uint64_t bd = tc::umma_desc_sw128(a_addr + A_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          tc::umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
-        tc::umma_commit(&ctl->empty[s]);
+          for (int k = 0; k < BK / 16; ++k)
+            tc::umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          tc::umma_commit(&ctl->empty[s]);
+        }
+        if (ok) tc::umma_commit(&ctl->tmem_full[b]);
+        u += kb1 - kb0;
       }
-      if (ok) {
-        tc::umma_commit(&ctl->accum);
-      } else {
-        raise_fault(ctl, fault);
-        tc::umma_commit(&ctl->drain);
-        tc::mbar_wait(&ctl->drain, 0, kWaitLimitNs, nullptr);
-      }
+      if (!ok) raise_fault(ctl, fault);
+      // every MMA issued has completed before TMEM is freed
+      tc::umma_commit(&ctl->drain);
+      tc::mbar_wait(&ctl->drain, 0, kWaitLimitNs, nullptr);
     }
   } else {
-    // ---- epilogue: TMEM -> rotate -> global ----------------------------
-    bool ready = tc::mbar_wait(&ctl->accum, 0, kWaitLimitNs, &ctl->abort);
-    ready = __all_sync(0xffffffffu, ready);
-    if (ready) {
+    // ---- epilogue: warp w drains TMEM lanes 32 (w % 4) .. +31, head w / 4 ----
+    const int quarter = warp % 4, hh = warp / 4;
+    const int row = quarter * 32 + lane;
+    int j = 0;
+    for (int64_t u = u_begin; u < u_end; ++j) {
+      const int64_t t = u / k_blocks;
+      const int kb0 = (int)(u - t * k_blocks);
+      const int kb1 = (int)min((int64_t)k_blocks, kb0 + (u_end - u));
+      u += kb1 - kb0;
+      const int b = j & 1;
+      const int mt = (int)(t % m_tiles), nt = (int)(t / m_tiles);
+      const int m0 = mt * BM, m = m0 + row;
+      const bool valid = m < num_tokens;
+      const int head = nt * (BN / HEAD) + hh;
+      const bool whole = kb0 == 0 && kb1 == k_blocks;
+      // the position (and cache row) is read while the MMAs run
+      const C* cs = whole ? cache_row(cache, positions, max_position, m, valid, head < rot_heads)
+                          : nullptr;
+      bool ready = tc::mbar_wait(&ctl->tmem_full[b], (uint32_t)(j >> 1) & 1u, kWaitLimitNs,
+                                 &ctl->abort);
+      ready = epi_all(ready);
+      if (!ready) {
+        raise_fault(ctl, fault);
+        break;
+      }
       tc::tc_fence_after();
-      const int r = warp * 32 + lane;
-      const int m = m0 + r;
-      const bool row_ok = m < num_tokens;
-      const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-      T* orow = out + (int64_t)(row_ok ? m : 0) * out_stride + n0;
-      bool rot = false;
-      const C* cs = cache;
-      if (row_ok && head < rot_heads) {
-        const int64_t pos = positions[m];
-        rot = pos >= 0 && pos < max_position;
-        if (rot) cs = cache + pos * BN;
+      const uint32_t taddr = tmem + (uint32_t)(b * BN + hh * HEAD) +
+                             (static_cast<uint32_t>(quarter * 32) << 16);
+      if (whole) {
+        T* o = out + (int64_t)(valid ? m : 0) * out_stride + (int64_t)head * HEAD;
+        finish_head_tmem<T, C, NEOX>(taddr, o, cs, valid && head < total_heads);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ctl->tmem_empty[b]);
+        continue;
       }
-      if (NEOX) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 16) {
-          uint32_t xr[16], yr[16];
-          tc::tmem_ld16(trow + c, xr);
-          tc::tmem_ld16(trow + BN / 2 + c, yr);
-          tc::tmem_wait_ld(xr);
-          tc::tmem_wait_ld(yr);
-          float x[16], y[16];
-          as_float(xr, x);
-          as_float(yr, y);
-          if (rot) {
-            float cv[16], sv[16], xo[16], yo[16];
-            load16(cs + c, cv);
-            load16(cs + BN / 2 + c, sv);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              xo[e] = x[e] * cv[e] - y[e] * sv[e];
-              yo[e] = y[e] * cv[e] + x[e] * sv[e];
-            }
-            if (row_ok) {
-              store16(orow + c, xo);
-              store16(orow + BN / 2 + c, yo);
-            }
-          } else if (row_ok) {
-            store16(orow + c, x);
-            store16(orow + BN / 2 + c, y);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t ar[16];
-          tc::tmem_ld16(trow + c, ar);
-          tc::tmem_wait_ld(ar);
-          float a[16];
-          as_float(ar, a);
-          if (rot) {
-            // pairs (c + 2p, c + 2p + 1) use cache entries c/2 + p
-            float cv[8], sv[8], o[16];
-            load8(cs + c / 2, cv);
-            load8(cs + BN / 2 + c / 2, sv);
-#pragma unroll
-            for (int p = 0; p < 8; ++p) {
-              o[2 * p] = a[2 * p] * cv[p] - a[2 * p + 1] * sv[p];
-              o[2 * p + 1] = a[2 * p + 1] * cv[p] + a[2 * p] * sv[p];
-            }
-            if (row_ok) store16(orow + c, o);
-          } else if (row_ok) {
-            store16(orow + c, a);
-          }
-        }
+      // a shared tile: store this CTA's partial, then count it
+      const int64_t seg_u0 = t * k_blocks + kb0;
+      const int my_slot = seg_u0 == u_begin ? 2 * cta : 2 * cta + 1;
+      store_partial(taddr, slots + (int64_t)my_slot * SLOT_FLOATS, hh, row, valid);
+      // the accumulator is free for the segment after next
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ctl->tmem_empty[b]);
+      // All epilogue threads' partial stores are ordered before thread 0's
+      // fence by the barrier; the fence (cumulative) then releases them at GPU
+      // scope before the count.  The CTA that completes the count fences
+      // again before its threads read the other partials.
+      epi_sync();
+      const int c0 = sp.owner(t * k_blocks), c1 = sp.owner(t * k_blocks + k_blocks - 1);
+      if (threadIdx.x == 0) {
+        __threadfence();
+        const int prev = atomicAdd(&counters[t], 1);
+        const int last = prev == c1 - c0;
+        if (last) counters[t] = 0;  // ready for the next call
+        __threadfence();
+        ctl->last = last;
       }
+      epi_sync();
+      const bool last = *reinterpret_cast<volatile int*>(&ctl->last) != 0;
+      epi_sync();  // ctl->last is rewritten by the next shared tile
+      if (last)
+        fixup_tile<T, C, NEOX>(slots, sp, t * k_blocks, c0, c1,
+                               out + (int64_t)m0 * out_stride + (int64_t)nt * BN, out_stride,
+                               cache, positions, max_position, m0,
+                               min(BM, num_tokens - m0), nt * (BN / HEAD), rot_heads,
+                               total_heads, warp, lane);
     }
   }
 
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, BN);
+  if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // ---------------------------------------------------------------- host ----
@@ -305,26 +527,52 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows,
   const cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
   const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                         2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: tensor map rejected (CUresult %d)", name, (int)r);
+  const CUresult r =
+      enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: tensor map rejected (CUresult %d)", name, (int)r);
   return PACE_OK;
+}
+
+// Workspace layout: 2 partial slots per SM (a fixed size for the device),
+// then one int32 counter per tile.  The counters sit at the same offset for
+// every shape, so a workspace that a call of one shape left zeroed is valid
+// for a call of any other shape that fits in it.
+struct QkvShape {
+  int m_tiles, n_tiles, k_blocks, ctas;
+  size_t slot_bytes, workspace_bytes;
+};
+
+QkvShape qkv_shape(int64_t num_tokens, int64_t hidden_size, int total_heads, int sms) {
+  QkvShape s;
+  s.m_tiles = (int)ceil_div(num_tokens, BM);
+  s.n_tiles = (int)ceil_div((int64_t)total_heads * HEAD, BN);
+  s.k_blocks = (int)ceil_div(hidden_size, BK);
+  const int64_t units = (int64_t)s.m_tiles * s.n_tiles * s.k_blocks;
+  s.ctas = (int)(units < sms ? units : sms);
+  s.slot_bytes = (size_t)2 * sms * SLOT_FLOATS * sizeof(float);
+  s.workspace_bytes =
+      s.slot_bytes + ((size_t)s.m_tiles * s.n_tiles * sizeof(int) + 255) / 256 * 256;
+  return s;
 }
 
 template <typename T, typename C, bool NEOX>
 int launch_qkv_rope(const CUtensorMap& ma, const CUtensorMap& mb, void* out, int64_t out_stride,
                     const int64_t* positions, const void* cache, int64_t max_position,
-                    int64_t num_tokens, int heads, int rot_heads, int k_blocks, int32_t* fault,
-                    int dev, cudaStream_t stream) {
+                    int64_t num_tokens, const QkvShape& sh, int rot_heads, int total_heads,
+                    void* workspace, int32_t* fault, int dev, cudaStream_t stream) {
   auto kernel = qkv_rope_kernel<T, C, NEOX>;
   cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), dev, SMEM_BYTES);
   if (err != cudaSuccess) return cuda_fail(err, "qkv_proj_rope (smem attribute)");
-  const dim3 grid((unsigned)ceil_div(num_tokens, BM), (unsigned)heads);
-  err = launch(kernel, grid, dim3(THREADS), SMEM_BYTES, stream, ma, mb, static_cast<T*>(out),
-               out_stride, positions, static_cast<const C*>(cache), max_position,
-               (int)num_tokens, rot_heads, k_blocks, fault);
+  float* slots = static_cast<float*>(workspace);
+  int* counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + sh.slot_bytes);
+  err = launch(kernel, dim3((unsigned)sh.ctas), dim3(THREADS), SMEM_BYTES, stream, ma, mb,
+               static_cast<T*>(out), out_stride, positions, static_cast<const C*>(cache),
+               max_position, (int)num_tokens, sh.m_tiles, sh.k_blocks, rot_heads, total_heads,
+               counters, slots, fault);
   if (err != cudaSuccess) return cuda_fail(err, "qkv_proj_rope");
   return PACE_OK;
 }
@@ -332,21 +580,33 @@ int launch_qkv_rope(const CUtensorMap& ma, const CUtensorMap& mb, void* out, int
 }  // namespace
 }  // namespace pace
 
+extern "C" size_t pace_qkv_proj_rope_workspace_size(int64_t num_tokens, int64_t hidden_size,
+                                                    int num_heads, int num_kv_heads,
+                                                    int device) {
+  using namespace pace;
+  if (num_tokens <= 0 || hidden_size <= 0 || num_heads < 0 || num_kv_heads < 0 ||
+      num_heads + num_kv_heads <= 0)
+    return 0;
+  return qkv_shape(num_tokens, hidden_size, num_heads + 2 * num_kv_heads, sm_count(device))
+      .workspace_bytes;
+}
+
 extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
                                   const int64_t* positions, int64_t num_tokens,
                                   int64_t hidden_size, int num_heads, int num_kv_heads,
                                   int head_size, int64_t hidden_row_stride,
                                   int64_t out_row_stride, const void* cos_sin_cache,
                                   int cache_dtype, int rot_dim, int64_t max_position, int is_neox,
-                                  int dtype, int32_t* fault_flags, cudaStream_t stream) {
+                                  int dtype, void* workspace, size_t workspace_bytes,
+                                  int32_t* fault_flags, cudaStream_t stream) {
   using namespace pace;
   const char* name = "qkv_proj_rope";
   if (num_tokens < 0 || num_tokens > INT32_MAX || hidden_size <= 0 || num_heads < 0 ||
       num_kv_heads < 0 || num_heads + num_kv_heads <= 0)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad shape", name);
-  if (head_size != BN || rot_dim != head_size)
+  if (head_size != HEAD || rot_dim != head_size)
     return fail(PACE_ERR_INVALID_ARGUMENT,
-                "%s: head_size and rot_dim must both be %d (got %d, %d)", name, BN, head_size,
+                "%s: head_size and rot_dim must both be %d (got %d, %d)", name, HEAD, head_size,
                 rot_dim);
   if (dtype != PACE_BF16 && dtype != PACE_F16)
     return fail(PACE_ERR_UNSUPPORTED_DTYPE, "%s: dtype %d must be bfloat16 or float16", name,
@@ -362,15 +622,22 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
   if (hidden_size % 8 != 0 || hidden_row_stride % 8 != 0 || out_row_stride % 8 != 0)
     return fail(PACE_ERR_INVALID_ARGUMENT,
                 "%s: hidden size and row strides must be multiples of 8 elements", name);
+  if (hidden_size > (int64_t)INT32_MAX * BK || num_tokens > (int64_t)1 << 24)
+    return fail(PACE_ERR_TOO_LARGE, "%s: shape too large", name);
   if (max_position <= 0) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: empty cos_sin_cache", name);
   if (num_tokens == 0) return PACE_OK;
-  if (!qkv_out || !hidden || !weight || !positions || !cos_sin_cache)
+  if (!qkv_out || !hidden || !weight || !positions || !cos_sin_cache || !workspace)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
-  if (!aligned16(qkv_out) || !aligned16(hidden) || !aligned16(weight) || !aligned16(cos_sin_cache))
-    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: pointers must be 16-byte aligned", name);
-  if (ceil_div(hidden_size, BK) > INT32_MAX)
-    return fail(PACE_ERR_TOO_LARGE, "%s: hidden size too large", name);
+  if (!aligned16(qkv_out) || !aligned16(hidden) || !aligned16(weight) ||
+      !aligned16(cos_sin_cache) || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: pointers must be 16-byte aligned (the workspace 256-byte aligned)", name);
   StreamDeviceGuard guard(stream);
+  const int dev = guard.device();
+  const QkvShape sh = qkv_shape(num_tokens, hidden_size, heads, sm_count(dev));
+  if (workspace_bytes < sh.workspace_bytes)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
+                workspace_bytes, sh.workspace_bytes);
   const bool bf16 = dtype == PACE_BF16;
   CUtensorMap ma, mb;
   int st = make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
@@ -378,16 +645,16 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
   st = make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
   if (st != PACE_OK) return st;
   const int rot_heads = num_heads + num_kv_heads;
-  const int kb = (int)ceil_div(hidden_size, BK);
-  const int dev = guard.device();
-#define PACE_QKV_ROPE(T, C, NX)                                                                  \
-  launch_qkv_rope<T, C, NX>(ma, mb, qkv_out, out_row_stride, positions, cos_sin_cache,          \
-                            max_position, num_tokens, heads, rot_heads, kb, fault_flags, dev, \
-                            stream)
+#define PACE_QKV_ROPE(T, C, NX)                                                                 \
+  launch_qkv_rope<T, C, NX>(ma, mb, qkv_out, out_row_stride, positions, cos_sin_cache,         \
+                            max_position, num_tokens, sh, rot_heads, heads, workspace,         \
+                            fault_flags, dev, stream)
   const bool neox = is_neox != 0;
   const bool f32c = cache_dtype == PACE_F32;
   if (bf16) {
-    if (f32c) return neox ? PACE_QKV_ROPE(__nv_bfloat16, float, true) : PACE_QKV_ROPE(__nv_bfloat16, float, false);
+    if (f32c)
+      return neox ? PACE_QKV_ROPE(__nv_bfloat16, float, true)
+                  : PACE_QKV_ROPE(__nv_bfloat16, float, false);
     return neox ? PACE_QKV_ROPE(__nv_bfloat16, __nv_bfloat16, true)
                 : PACE_QKV_ROPE(__nv_bfloat16, __nv_bfloat16, false);
   }

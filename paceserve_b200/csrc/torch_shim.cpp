@@ -12,6 +12,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -184,10 +186,24 @@ void rotary_embedding(Tensor& positions, Tensor& query, Tensor& key, int64_t hea
 // replaces qkv_proj followed by rotary_embedding
 // (paceserve/model_executor/models/llama.py:176-178); `qkv` is the [T, (nq +
 // 2 nkv) * head_size] output the split into q, k, v views reads.
+// The stream-K workspace of the fused projection, kept per (device, stream):
+// zero-filled once on that stream, and left zeroed by every call, so calls on
+// one stream can share it; calls on different streams never do.
+Tensor qkv_workspace(const at::Device& dev, cudaStream_t stream, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, Tensor> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  Tensor& ws = cache[{dev.index(), stream}];
+  if (!ws.defined() || (size_t)ws.numel() < bytes)
+    ws = at::zeros({(int64_t)bytes}, at::TensorOptions().dtype(at::kByte).device(dev));
+  return ws;
+}
+
 void qkv_proj_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& weight, Tensor& positions,
                                int64_t head_size, int64_t num_heads, int64_t num_kv_heads,
                                Tensor& cos_sin_cache, bool is_neox,
-                               const c10::optional<Tensor>& fault_flags) {
+                               const c10::optional<Tensor>& fault_flags,
+                               const c10::optional<Tensor>& workspace) {
   const char* op = "qkv_proj_rotary_embedding";
   check_cuda(hidden, op, "hidden");
   check_same_device(qkv, hidden, op);
@@ -218,12 +234,27 @@ void qkv_proj_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& weight, Tens
               " entries for ", h.rows, " tokens");
   const at::cuda::CUDAGuard guard(hidden.device());
   int32_t* fault = counter_ptr(fault_flags, hidden.device(), op, "fault_flags");
+  if (h.rows == 0) return;
+  const cudaStream_t stream = stream_of(hidden);
+  const size_t need = pace_qkv_proj_rope_workspace_size(h.rows, h.width, (int)num_heads,
+                                                        (int)num_kv_heads, hidden.device().index());
+  Tensor ws;
+  if (workspace.has_value()) {
+    ws = *workspace;
+    TORCH_CHECK(ws.is_cuda() && ws.device() == hidden.device() && ws.is_contiguous() &&
+                    (size_t)ws.nbytes() >= need,
+                op, ": workspace must be a contiguous tensor of at least ", need, " bytes on ",
+                hidden.device());
+  } else {
+    ws = qkv_workspace(hidden.device(), stream, need);
+  }
   check_status(pace_qkv_proj_rope(qkv.data_ptr(), hidden.data_ptr(), weight.data_ptr(),
                                   positions.data_ptr<int64_t>(), h.rows, h.width, (int)num_heads,
                                   (int)num_kv_heads, (int)head_size, h.stride, o.stride,
                                   cos_sin_cache.data_ptr(), pace_dtype(cos_sin_cache),
                                   (int)cos_sin_cache.size(1), cos_sin_cache.size(0),
-                                  is_neox ? 1 : 0, pace_dtype(hidden), fault, stream_of(hidden)),
+                                  is_neox ? 1 : 0, pace_dtype(hidden), ws.data_ptr(),
+                                  (size_t)ws.nbytes(), fault, stream),
                op);
 }
 
@@ -686,7 +717,17 @@ PYBIND11_MODULE(_C, m) {
          "q and k heads before rounding (fused qkv_proj + rotary_embedding).",
          py::arg("qkv"), py::arg("hidden"), py::arg("weight"), py::arg("positions"),
          py::arg("head_size"), py::arg("num_heads"), py::arg("num_kv_heads"),
-         py::arg("cos_sin_cache"), py::arg("is_neox"), py::arg("fault_flags") = py::none());
+         py::arg("cos_sin_cache"), py::arg("is_neox"), py::arg("fault_flags") = py::none(),
+         py::arg("workspace") = py::none());
+  pe.def("qkv_proj_rope_workspace_size",
+         [](int64_t num_tokens, int64_t hidden_size, int64_t num_heads, int64_t num_kv_heads,
+            int64_t device) {
+           return pace_qkv_proj_rope_workspace_size(num_tokens, hidden_size, (int)num_heads,
+                                                    (int)num_kv_heads, (int)device);
+         },
+         "Bytes of zero-filled workspace qkv_proj_rotary_embedding needs for this shape.",
+         py::arg("num_tokens"), py::arg("hidden_size"), py::arg("num_heads"),
+         py::arg("num_kv_heads"), py::arg("device"));
 
   auto act = m.def_submodule("activation_ops");
   act.def("silu_and_mul", &silu_and_mul, "Activation function used in SwiGLU.", py::arg("out"),

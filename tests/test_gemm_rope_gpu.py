@@ -160,19 +160,81 @@ def test_graph_capture_and_repeat():
     check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
 
 
-def test_c_abi_direct_call():
+def test_c_abi_direct_call_and_workspace_reuse():
     lib = cabi.load()
     T, H, nq, nkv, hd = 64, 256, 2, 1, 128
     hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, 2)
     hd_, wd, pd, cd = hidden.to(DEV), weight.to(DEV), positions.to(DEV), cache.to(DEV)
     n = (nq + 2 * nkv) * hd
-    out = torch.empty(T, n, dtype=torch.bfloat16, device=DEV)
-    st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(), T, H,
-                                nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd, 8192, 1,
-                                cabi.PACE_BF16, None, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    assert st == cabi.PACE_OK, lib.pace_last_error()
+    need = lib.pace_qkv_proj_rope_workspace_size(T, H, nq, nkv, 0)
+    assert need == pos_encoding_ops.qkv_proj_rope_workspace_size(T, H, nq, nkv, 0) > 0
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    ref = reference(hidden, weight, positions, nq, nkv, hd, cache, True)
+    for _ in range(3):  # the workspace is left zeroed: reusable without clearing
+        out = torch.empty(T, n, dtype=torch.bfloat16, device=DEV)
+        st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(),
+                                    T, H, nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd,
+                                    8192, 1, cabi.PACE_BF16, ws.data_ptr(), need, None, stream)
+        assert st == cabi.PACE_OK, lib.pace_last_error()
+        torch.cuda.synchronize()
+        check(out, ref, torch.bfloat16)
+    # the tile counters at the end of the workspace are back at zero
+    assert int(ws[-256:].sum().item()) == 0
+    st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(), T,
+                                H, nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd, 8192, 1,
+                                cabi.PACE_BF16, ws.data_ptr(), need - 1, None, stream)
+    assert st == cabi.PACE_ERR_INVALID_ARGUMENT
+    assert b"workspace" in lib.pace_last_error()
+
+
+def test_caller_workspace_through_the_shim():
+    T, H, nq, nkv, hd = 700, 1024, 8, 2, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, 12)
+    need = pos_encoding_ops.qkv_proj_rope_workspace_size(T, H, nq, nkv, 0)
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden.to(DEV), weight.to(DEV),
+                                               positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                               True, None, ws)
     torch.cuda.synchronize()
-    check(out, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
+    with pytest.raises(RuntimeError, match="workspace"):
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden.to(DEV), weight.to(DEV),
+                                                   positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                                   True, None, ws[: need // 2])
+
+
+def test_one_workspace_across_shapes():
+    """A zeroed workspace stays valid when calls of different shapes (different
+    tile counts) share it, in either order."""
+    nq, nkv, hd, H = 8, 2, 128, 1024
+    need = max(pos_encoding_ops.qkv_proj_rope_workspace_size(T, H, nq, nkv, 0)
+               for T in (1, 300, 1500))
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    for T in (1, 1500, 300, 1, 300, 1500):
+        hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, T)
+        qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden.to(DEV), weight.to(DEV),
+                                                   positions.to(DEV), hd, nq, nkv,
+                                                   cache.to(DEV), False, None, ws)
+        torch.cuda.synchronize()
+        check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, False),
+              torch.bfloat16)
+
+
+@pytest.mark.parametrize("T,H,nq,nkv", [(1, 8192, 64, 8), (2048, 4096, 32, 8), (333, 4096, 3, 1)])
+def test_larger_and_odd_head_counts(T, H, nq, nkv):
+    # 70B-wide rows at one token (every tile shared by many CTAs), a long
+    # prefill, and an odd head count (the last tile's second head is absent)
+    hd = 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, T + nq)
+    qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hidden.to(DEV), weight.to(DEV),
+                                               positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                               True)
+    torch.cuda.synchronize()
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
 
 
 def test_rejected_shapes():
