@@ -120,6 +120,29 @@ int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
                        int64_t max_position, int is_neox, int dtype, void* workspace,
                        size_t workspace_bytes, int32_t* fault_flags, cudaStream_t stream);
 
+/* Allocation-free variant of pace_qkv_proj_rope.  No counterpart in the
+ * reference.  For callers that cannot allocate device memory: a plugin host
+ * that hands an op only its input and output buffers, or a latency-bound
+ * serving loop that must not call cudaMalloc (it synchronises the device).
+ * Same arguments and results as pace_qkv_proj_rope, without the workspace:
+ * its scratch is a fixed array inside this library (15.8 MiB, held by every
+ * GPU that loads the library until the process exits), so it runs at most 63
+ * CTAs (slower than the workspace version) and rejects shapes of more than
+ * 16384 output tiles of 128 x 256 (PACE_ERR_TOO_LARGE).  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  Every call shares the array:
+ * calls that may overlap on the GPU (other streams, other host threads) race
+ * and must be serialised by the caller.  Each call clears the tile counters
+ * it uses on its stream (cudaMemsetAsync) before the kernel; it allocates
+ * nothing. */
+int pace_qkv_proj_rope_no_alloc(void* qkv_out, const void* hidden, const void* weight,
+                                const int64_t* positions, int64_t num_tokens,
+                                int64_t hidden_size, int num_heads, int num_kv_heads,
+                                int head_size, int64_t hidden_row_stride,
+                                int64_t out_row_stride, const void* cos_sin_cache,
+                                int cache_dtype, int rot_dim, int64_t max_position, int is_neox,
+                                int dtype, int32_t* fault_flags, cudaStream_t stream);
+
 /* ---- gated and element-wise activations ---------------------------------
  * *_and_mul: input [T, 2d] -> out [T, d], out = act(x[:, :d]) * x[:, d:].
  * Replaces silu_and_mul (csrc/activation.cpp:3-13,

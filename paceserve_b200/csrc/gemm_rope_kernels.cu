@@ -30,6 +30,8 @@
 // the other.  Every mbarrier wait is bounded by %globaltimer; on expiry the
 // CTA records bit 30 in the caller's fault word, stops issuing, waits (bounded
 // again) for its own copies and MMAs, frees TMEM and returns.
+#include <mutex>
+
 #include "tcgen05.cuh"
 
 namespace pace {
@@ -661,4 +663,133 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
   if (f32c) return neox ? PACE_QKV_ROPE(__half, float, true) : PACE_QKV_ROPE(__half, float, false);
   return neox ? PACE_QKV_ROPE(__half, __half, true) : PACE_QKV_ROPE(__half, __half, false);
 #undef PACE_QKV_ROPE
+}
+
+// ------------------------------------------------- allocation-free variant --
+// Some callers cannot allocate device memory for a workspace: a plugin host
+// that hands an op only its input and output buffers, or a latency-bound
+// serving loop that must not call cudaMalloc (it synchronises the device).
+// pace_qkv_proj_rope_no_alloc serves them with scratch in this file-scope
+// array instead: partial slots for up to kNoAllocCtas CTAs (the variant runs
+// at most that many, about 43 % of a B200's SMs) and counters for up to
+// kNoAllocTiles output tiles.  Every GPU that loads this code holds the array
+// (15.8 MiB) until the process exits.
+namespace pace {
+namespace {
+constexpr int kNoAllocCtas = 63;
+constexpr int kNoAllocTiles = 16384;
+constexpr size_t kNoAllocSlotBytes = (size_t)2 * kNoAllocCtas * SLOT_FLOATS * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocSlotBytes + (size_t)kNoAllocTiles * sizeof(int);
+constexpr int kMaxDevices = 64;
+}  // namespace
+}  // namespace pace
+
+static __device__ __align__(256) unsigned char g_qkv_no_alloc_scratch[pace::kNoAllocBytes];
+
+namespace pace {
+namespace {
+// Device address of the scratch array on the current device `dev`, looked up
+// once per device (cudaGetSymbolAddress; the host-side name is not a device
+// address).  nullptr on failure, with the error recorded.
+void* no_alloc_scratch(int dev) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) {
+    fail(PACE_ERR_INVALID_ARGUMENT, "qkv_proj_rope_no_alloc: device %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_qkv_no_alloc_scratch);
+    if (err != cudaSuccess) {
+      cuda_fail(err, "qkv_proj_rope_no_alloc (scratch address)");
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+}  // namespace
+}  // namespace pace
+
+extern "C" int pace_qkv_proj_rope_no_alloc(
+    void* qkv_out, const void* hidden, const void* weight, const int64_t* positions,
+    int64_t num_tokens, int64_t hidden_size, int num_heads, int num_kv_heads, int head_size,
+    int64_t hidden_row_stride, int64_t out_row_stride, const void* cos_sin_cache,
+    int cache_dtype, int rot_dim, int64_t max_position, int is_neox, int dtype,
+    int32_t* fault_flags, cudaStream_t stream) {
+  using namespace pace;
+  const char* name = "qkv_proj_rope_no_alloc";
+  if (num_tokens < 0 || num_tokens > INT32_MAX || hidden_size <= 0 || num_heads < 0 ||
+      num_kv_heads < 0 || num_heads + num_kv_heads <= 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad shape", name);
+  if (head_size != HEAD || rot_dim != head_size)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: head_size and rot_dim must both be %d (got %d, %d)", name, HEAD, head_size,
+                rot_dim);
+  if (dtype != PACE_BF16 && dtype != PACE_F16)
+    return fail(PACE_ERR_UNSUPPORTED_DTYPE, "%s: dtype %d must be bfloat16 or float16", name,
+                dtype);
+  if (cache_dtype != PACE_F32 && cache_dtype != dtype)
+    return fail(PACE_ERR_UNSUPPORTED_DTYPE,
+                "%s: cos_sin_cache dtype %d must be float32 or the q/k dtype %d", name,
+                cache_dtype, dtype);
+  const int heads = num_heads + 2 * num_kv_heads;
+  const int64_t n = (int64_t)heads * head_size;
+  if (hidden_row_stride < hidden_size || out_row_stride < n)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: row stride smaller than the row", name);
+  if (hidden_size % 8 != 0 || hidden_row_stride % 8 != 0 || out_row_stride % 8 != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: hidden size and row strides must be multiples of 8 elements", name);
+  if (hidden_size > (int64_t)INT32_MAX * BK || num_tokens > (int64_t)1 << 24)
+    return fail(PACE_ERR_TOO_LARGE, "%s: shape too large", name);
+  const int64_t tiles = ceil_div(num_tokens, BM) * ceil_div(n, BN);
+  if (tiles > kNoAllocTiles)
+    return fail(PACE_ERR_TOO_LARGE,
+                "%s: %lld output tiles of %dx%d exceed the fixed scratch's %d (use "
+                "pace_qkv_proj_rope with a workspace)",
+                name, (long long)tiles, BM, BN, kNoAllocTiles);
+  if (max_position <= 0) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: empty cos_sin_cache", name);
+  if (num_tokens == 0) return PACE_OK;
+  if (!qkv_out || !hidden || !weight || !positions || !cos_sin_cache)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(qkv_out) || !aligned16(hidden) || !aligned16(weight) || !aligned16(cos_sin_cache))
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: pointers must be 16-byte aligned", name);
+  StreamDeviceGuard guard(stream);
+  const int dev = guard.device();
+  void* scratch = no_alloc_scratch(dev);
+  if (!scratch) return PACE_ERR_CUDA;
+  QkvShape sh = qkv_shape(num_tokens, hidden_size, heads, sm_count(dev));
+  if (sh.ctas > kNoAllocCtas) sh.ctas = kNoAllocCtas;
+  sh.slot_bytes = kNoAllocSlotBytes;
+  // The counters must start at zero.  Calls leave them zero, but one whose
+  // wait expired may not: clear them on the stream first (no allocation).
+  cudaError_t err = cudaMemsetAsync(static_cast<char*>(scratch) + kNoAllocSlotBytes, 0,
+                                    (size_t)tiles * sizeof(int), stream);
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  const bool bf16 = dtype == PACE_BF16;
+  CUtensorMap ma, mb;
+  int st = make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
+  if (st != PACE_OK) return st;
+  st = make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
+  if (st != PACE_OK) return st;
+  const int rot_heads = num_heads + num_kv_heads;
+#define PACE_QKV_ROPE_NA(T, C, NX)                                                               \
+  launch_qkv_rope<T, C, NX>(ma, mb, qkv_out, out_row_stride, positions, cos_sin_cache,         \
+                            max_position, num_tokens, sh, rot_heads, heads, scratch,           \
+                            fault_flags, dev, stream)
+  const bool neox = is_neox != 0;
+  const bool f32c = cache_dtype == PACE_F32;
+  if (bf16) {
+    if (f32c)
+      return neox ? PACE_QKV_ROPE_NA(__nv_bfloat16, float, true)
+                  : PACE_QKV_ROPE_NA(__nv_bfloat16, float, false);
+    return neox ? PACE_QKV_ROPE_NA(__nv_bfloat16, __nv_bfloat16, true)
+                : PACE_QKV_ROPE_NA(__nv_bfloat16, __nv_bfloat16, false);
+  }
+  if (f32c)
+    return neox ? PACE_QKV_ROPE_NA(__half, float, true) : PACE_QKV_ROPE_NA(__half, float, false);
+  return neox ? PACE_QKV_ROPE_NA(__half, __half, true) : PACE_QKV_ROPE_NA(__half, __half, false);
+#undef PACE_QKV_ROPE_NA
 }
