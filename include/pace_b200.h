@@ -202,6 +202,40 @@ int pace_moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel
                               int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
                               int fill_padding, cudaStream_t stream);
 
+/* ---- MoE expert GEMMs (tcgen05) -----------------------------------------
+ * The expert computation of fused_experts
+ * (paceserve/model_executor/layers/fused_moe/fused_moe.py:411-544: the Triton
+ * fused_moe_kernel at :16-148 with w1, silu_and_mul, then with w2 and
+ * MUL_ROUTED_WEIGHT), over the routing of pace_moe_align_block_size with
+ * block_size 128: sorted_token_ids [num_sorted] (padding id = numel =
+ * T * top_k), expert_ids [num_sorted / 128], num_tokens_post_pad [1], all on
+ * the device.  dtype in {F16, BF16}; rows 16-byte aligned, widths and row
+ * strides multiples of 8 elements.
+ *
+ * pace_moe_gather_rows: out[i] = in[sorted_token_ids[i] / top_k] for
+ * i < num_tokens_post_pad, zero rows for padding ids; rows past the padded
+ * total are left untouched. */
+int pace_moe_gather_rows(void* out, const void* in, const int32_t* sorted_token_ids,
+                         int64_t num_sorted, const int32_t* num_tokens_post_pad, int64_t numel,
+                         int top_k, int64_t hidden, int64_t in_row_stride,
+                         int64_t out_row_stride, int dtype, cudaStream_t stream);
+/* pace_moe_gemm, mode 0: out[i, :n] = silu(a[i] @ w[e, :n]^T) * (a[i] @ w[e, n:2n]^T)
+ *   for the sorted rows i < num_tokens_post_pad, e = expert_ids[i / 128]; w is
+ *   the contiguous [E, 2n, k] gate/up weight (w1), out is [num_sorted, n].
+ *   SiLU in fp32 on the fp32 accumulator, one rounding.  n % 128 == 0.
+ * mode 1: out[id, :n] = topk_weights[id] * (a[i] @ w[e]^T) with id =
+ *   sorted_token_ids[i] < numel; w is the contiguous [E, n, k] weight (w2), out
+ *   is [numel, n] (the reference's intermediate_cache3).  n % 256 == 0.
+ * a is [num_sorted, k] in sorted order (mode 0: pace_moe_gather_rows output;
+ * mode 1: the mode 0 output).  fault_flags (optional device int32): bit 30 is
+ * OR-ed in when a bounded device wait expires. */
+int pace_moe_gemm(void* out, const void* a, const void* w, int64_t num_sorted,
+                  const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                  const int32_t* num_tokens_post_pad, int64_t numel, const float* topk_weights,
+                  int num_experts, int64_t n, int64_t k, int64_t a_row_stride,
+                  int64_t out_row_stride, int mode, int dtype, int32_t* fault_flags,
+                  cudaStream_t stream);
+
 /* ---- paged-KV block transfer --------------------------------------------
  * A KV cache is one tensor per layer, [num_blocks, 2, block_size, kv_heads,
  * head_dim], so block b of layer l is the contiguous slab of block_bytes

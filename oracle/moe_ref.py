@@ -136,3 +136,34 @@ def moe_align_block_size_c(topk_ids: np.ndarray, num_experts: int, block_size: i
         raise RuntimeError(f"moe_align_block_size_ref returned {rc}")
     t = int(total[0])
     return sorted_ids, expert_ids[: t // block_size].copy(), t
+
+
+# ----------------------------------------------------------- fused experts --
+def fused_experts_fp32(hidden, w1, w2, topk_weights, topk_ids):
+    """fp32 restatement of fused_experts
+    (paceserve/model_executor/layers/fused_moe/fused_moe.py:411-544) from the
+    same 16-bit inputs: for every token t and slot j with expert
+    e = topk_ids[t, j], y = silu(h W1[e, :I]^T) * (h W1[e, I:]^T) (the first
+    fused_moe_kernel launch, then silu_and_mul at :518-520), z = topk_weights[t, j]
+    * (y W2[e]^T) (the second launch with MUL_ROUTED_WEIGHT, :138-140), and
+    out[t] = sum_j z (:539-543).  torch tensors in, fp32 [T, H] out; done per
+    expert over the tokens routed to it."""
+    import torch
+
+    h = hidden.float()
+    w1f, w2f = w1.float(), w2.float()
+    inter = w1.shape[1] // 2
+    T, k = topk_ids.shape
+    out = torch.zeros(T, w2.shape[1], dtype=torch.float32)
+    ids = topk_ids.long()
+    tw = topk_weights.float()
+    for e in range(w1.shape[0]):
+        tok, slot = (ids == e).nonzero(as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        x = h[tok]
+        gu = x @ w1f[e].t()
+        y = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+        z = (y @ w2f[e].t()) * tw[tok, slot][:, None]
+        out.index_add_(0, tok, z)
+    return out

@@ -49,6 +49,7 @@ CUDA_SOURCES = [
     "kv_transfer_kernels.cu",
     "kv_append_kernels.cu",
     "gemm_rope_kernels.cu",
+    "moe_gemm_kernels.cu",
 ]
 
 

@@ -75,6 +75,33 @@ struct Split {
   }
 };
 
+// A CTA's segments, in order: first whole tiles cta, cta + ctas, ... of the
+// rounds that every CTA can fill (data-parallel), then its stream-K range of
+// the units of the tiles left over.  Tiles are numbered n fastest, so the
+// CTAs running together read a few rows of A and the whole weight, which
+// stays in L2, instead of every tile of both.
+struct Walk {
+  int64_t t_next, t_stop, step;  // data-parallel tiles t_next, +step, ... < t_stop
+  int64_t u, u_end;              // stream-K units, relative to tile t_stop
+  int k_blocks;
+  __device__ __forceinline__ bool next(int64_t& t, int& kb0, int& kb1) {
+    if (t_next < t_stop) {
+      t = t_next;
+      t_next += step;
+      kb0 = 0;
+      kb1 = k_blocks;
+      return true;
+    }
+    if (u >= u_end) return false;
+    const int64_t rt = u / k_blocks;
+    t = t_stop + rt;
+    kb0 = (int)(u - rt * k_blocks);
+    kb1 = (int)min((int64_t)k_blocks, kb0 + (u_end - u));
+    u += kb1 - kb0;
+    return true;
+  }
+};
+
 __device__ __forceinline__ void raise_fault(Ctl* ctl, int32_t* fault) {
   *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
   if (fault) atomicOr(fault, kFaultTimeout);
@@ -274,8 +301,18 @@ __device__ __forceinline__ void fixup_tile(const float* slots, const Split& sp, 
   if (head >= total_heads) return;
   const bool rotated = head < rot_heads;
   const int ca = hh * 8 + col_a<NEOX>(i) / 16, cb = hh * 8 + col_b<NEOX>(i) / 16;
-  for (int r = lane; r < valid_rows; r += 32) {
-    const C* cs = cache_row(cache, positions, max_position, m0 + r, true, rotated);
+  // the four rows' positions first, so their loads overlap
+  const C* rows_cs[BM / 32];
+#pragma unroll
+  for (int p = 0; p < BM / 32; ++p) {
+    const int r = lane + 32 * p;
+    rows_cs[p] = cache_row(cache, positions, max_position, m0 + r, r < valid_rows, rotated);
+  }
+#pragma unroll
+  for (int p = 0; p < BM / 32; ++p) {
+    const int r = lane + 32 * p;
+    if (r >= valid_rows) break;
+    const C* cs = rows_cs[p];
     float a[16], b[16], cv[16], sv[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
@@ -311,11 +348,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
   const int n_tiles = (total_heads * HEAD + BN - 1) / BN;
-  Split sp;
-  sp.units = (int64_t)m_tiles * n_tiles * k_blocks;
+  const int64_t n_all = (int64_t)m_tiles * n_tiles;
+  const int64_t t_stop = n_all / gridDim.x * gridDim.x;  // first stream-K tile
+  Split sp;  // stream-K split of the units of tiles [t_stop, n_all)
+  sp.units = (n_all - t_stop) * k_blocks;
   sp.ctas = gridDim.x;
   sp.k_blocks = k_blocks;
-  const int64_t u_begin = sp.start(cta), u_end = sp.start(cta + 1);
+  const int64_t u_begin = sp.units > 0 ? sp.start(cta) : 0;
+  const int64_t u_end = sp.units > 0 ? sp.start(cta + 1) : 0;
+  const Walk walk0{cta, t_stop, (int64_t)gridDim.x, u_begin, u_end, k_blocks};
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
@@ -349,11 +390,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       int64_t i = 0;
       bool ok = true;
-      for (int64_t u = u_begin; u < u_end && ok;) {
-        const int64_t t = u / k_blocks;
-        const int kb0 = (int)(u - t * k_blocks);
-        const int kb1 = (int)min((int64_t)k_blocks, kb0 + (u_end - u));
-        const int m0 = (int)(t % m_tiles) * BM, n0 = (int)(t / m_tiles) * BN;
+      Walk walk = walk0;
+      int64_t t;
+      int kb0, kb1;
+      while (ok && walk.next(t, kb0, kb1)) {
+        const int m0 = (int)(t / n_tiles) * BM, n0 = (int)(t % n_tiles) * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++i) {
           const int s = (int)(i % STAGES);
           const uint32_t use = (uint32_t)(i / STAGES);
@@ -367,7 +408,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc::tma_load_2d(a, &tm_a, kb * BK, m0, &ctl->full[s]);
           tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
         }
-        u += kb1 - kb0;
       }
       if (!ok) raise_fault(ctl, fault);
       // every copy issued has landed before the CTA's shared memory is released
@@ -384,10 +424,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int64_t i = 0;
       int j = 0;
       bool ok = true;
-      for (int64_t u = u_begin; u < u_end && ok; ++j) {
-        const int64_t t = u / k_blocks;
-        const int kb0 = (int)(u - t * k_blocks);
-        const int kb1 = (int)min((int64_t)k_blocks, kb0 + (u_end - u));
+      Walk walk = walk0;
+      int64_t t;
+      int kb0, kb1;
+      for (; ok && walk.next(t, kb0, kb1); ++j) {
         const int b = j & 1;
         const uint32_t use_b = (uint32_t)(j >> 1);
         if (use_b > 0 &&
@@ -414,7 +454,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc::umma_commit(&ctl->empty[s]);
         }
         if (ok) tc::umma_commit(&ctl->tmem_full[b]);
-        u += kb1 - kb0;
       }
       if (!ok) raise_fault(ctl, fault);
       // every MMA issued has completed before TMEM is freed
@@ -426,13 +465,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp % 4, hh = warp / 4;
     const int row = quarter * 32 + lane;
     int j = 0;
-    for (int64_t u = u_begin; u < u_end; ++j) {
-      const int64_t t = u / k_blocks;
-      const int kb0 = (int)(u - t * k_blocks);
-      const int kb1 = (int)min((int64_t)k_blocks, kb0 + (u_end - u));
-      u += kb1 - kb0;
+    Walk walk = walk0;
+    int64_t t;
+    int kb0, kb1;
+    for (; walk.next(t, kb0, kb1); ++j) {
       const int b = j & 1;
-      const int mt = (int)(t % m_tiles), nt = (int)(t / m_tiles);
+      const int mt = (int)(t / n_tiles), nt = (int)(t % n_tiles);
       const int m0 = mt * BM, m = m0 + row;
       const bool valid = m < num_tokens;
       const int head = nt * (BN / HEAD) + hh;
@@ -459,8 +497,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         continue;
       }
       // a shared tile: store this CTA's partial, then count it
-      const int64_t seg_u0 = t * k_blocks + kb0;
-      const int my_slot = seg_u0 == u_begin ? 2 * cta : 2 * cta + 1;
+      const int64_t tile_u0 = (t - t_stop) * k_blocks;  // stream-K units are relative
+      const int my_slot = tile_u0 + kb0 == u_begin ? 2 * cta : 2 * cta + 1;
       store_partial(taddr, slots + (int64_t)my_slot * SLOT_FLOATS, hh, row, valid);
       // the accumulator is free for the segment after next
       tc::tc_fence_before();
@@ -471,7 +509,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // scope before the count.  The CTA that completes the count fences
       // again before its threads read the other partials.
       epi_sync();
-      const int c0 = sp.owner(t * k_blocks), c1 = sp.owner(t * k_blocks + k_blocks - 1);
+      const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + k_blocks - 1);
       if (threadIdx.x == 0) {
         __threadfence();
         const int prev = atomicAdd(&counters[t], 1);
@@ -484,7 +522,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool last = *reinterpret_cast<volatile int*>(&ctl->last) != 0;
       epi_sync();  // ctl->last is rewritten by the next shared tile
       if (last)
-        fixup_tile<T, C, NEOX>(slots, sp, t * k_blocks, c0, c1,
+        fixup_tile<T, C, NEOX>(slots, sp, tile_u0, c0, c1,
                                out + (int64_t)m0 * out_stride + (int64_t)nt * BN, out_stride,
                                cache, positions, max_position, m0,
                                min(BM, num_tokens - m0), nt * (BN / HEAD), rot_heads,
@@ -498,47 +536,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------- host ----
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled from the driver, looked up once (no link-time
-// dependency on libcuda).
-EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
-            cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return static_cast<EncodeTiledFn>(nullptr);
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
-// K-major [rows, cols] 16-bit matrix with a row stride, boxes of
-// box_rows x 64 elements, 128-byte swizzle.  Rows and columns past the end
-// read as zero.
-int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows, int64_t cols,
-                    int64_t row_stride, int box_rows, const char* name) {
-  EncodeTiledFn enc = encode_tiled();
-  if (!enc) return fail(PACE_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", name);
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r =
-      enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: tensor map rejected (CUresult %d)", name, (int)r);
-  return PACE_OK;
-}
-
 // Workspace layout: 2 partial slots per SM (a fixed size for the device),
 // then one int32 counter per tile.  The counters sit at the same offset for
 // every shape, so a workspace that a call of one shape left zeroed is valid
@@ -642,9 +639,9 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
                 workspace_bytes, sh.workspace_bytes);
   const bool bf16 = dtype == PACE_BF16;
   CUtensorMap ma, mb;
-  int st = make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
+  int st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
   if (st != PACE_OK) return st;
-  st = make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
+  st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
   if (st != PACE_OK) return st;
   const int rot_heads = num_heads + num_kv_heads;
 #define PACE_QKV_ROPE(T, C, NX)                                                                 \
@@ -770,9 +767,9 @@ extern "C" int pace_qkv_proj_rope_no_alloc(
   if (err != cudaSuccess) return cuda_fail(err, name);
   const bool bf16 = dtype == PACE_BF16;
   CUtensorMap ma, mb;
-  int st = make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
+  int st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
   if (st != PACE_OK) return st;
-  st = make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
+  st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
   if (st != PACE_OK) return st;
   const int rot_heads = num_heads + num_kv_heads;
 #define PACE_QKV_ROPE_NA(T, C, NX)                                                               \

@@ -169,5 +169,47 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[N]) {
   for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
 
+// ------------------------------------------------------------ tensor maps --
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, looked up once (no link-time
+// dependency on libcuda).
+inline EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// K-major [rows, cols] 16-bit matrix with a row stride, boxes of
+// box_rows x 64 elements (one 128-byte swizzle atom of K), 128-byte swizzle.  Rows and columns past the end
+// read as zero.
+inline int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows,
+                           int64_t cols, int64_t row_stride, int box_rows, const char* name) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(PACE_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", name);
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: tensor map rejected (CUresult %d)", name, (int)r);
+  return PACE_OK;
+}
+
 }  // namespace tc
 }  // namespace pace

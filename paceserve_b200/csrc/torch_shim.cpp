@@ -353,6 +353,90 @@ void moe_align_block_size(Tensor topk_ids, int64_t num_experts, int64_t block_si
                op);
 }
 
+// Rows of the routed tokens in moe_align order (block 128): out[i] =
+// input[sorted_token_ids[i] / top_k], zero for padding ids (>= numel).
+void moe_gather_rows(Tensor& out, Tensor& input, Tensor& sorted_token_ids,
+                     Tensor& num_tokens_post_pad, int64_t numel, int64_t top_k) {
+  const char* op = "moe_gather_rows";
+  check_cuda(input, op, "input");
+  for (const Tensor* t : {&out, &sorted_token_ids, &num_tokens_post_pad})
+    check_same_device(*t, input, op);
+  TORCH_CHECK(input.scalar_type() == at::kBFloat16 || input.scalar_type() == at::kHalf, op,
+              ": input must be bfloat16 or float16");
+  TORCH_CHECK(out.scalar_type() == input.scalar_type(), op, ": out and input dtypes differ");
+  TORCH_CHECK(sorted_token_ids.scalar_type() == at::kInt && sorted_token_ids.is_contiguous() &&
+                  num_tokens_post_pad.scalar_type() == at::kInt,
+              op, ": sorted_token_ids and num_tokens_post_pad must be contiguous int32");
+  TORCH_CHECK(input.dim() == 2 && out.dim() == 2 && out.size(1) == input.size(1), op,
+              ": input [T, H] and out [num_sorted, H] expected");
+  TORCH_CHECK(out.size(0) <= sorted_token_ids.numel(), op,
+              ": out has more rows than sorted_token_ids");
+  const Rows in = rows_of(input, op, "input");
+  const Rows o = rows_of(out, op, "out");
+  TORCH_CHECK(numel <= in.rows * top_k && top_k > 0, op, ": numel exceeds the input's rows");
+  const at::cuda::CUDAGuard guard(input.device());
+  check_status(pace_moe_gather_rows(out.data_ptr(), input.data_ptr(),
+                                    sorted_token_ids.data_ptr<int32_t>(), o.rows,
+                                    num_tokens_post_pad.data_ptr<int32_t>(), numel, (int)top_k,
+                                    in.width, in.stride, o.stride, pace_dtype(input),
+                                    stream_of(input)),
+               op);
+}
+
+// One expert GEMM of fused_experts on the tensor cores.  mode 0: out
+// [num_sorted, I] = silu(a @ w1[e, :I]^T) * (a @ w1[e, I:]^T), w = w1 [E, 2I, K];
+// mode 1: out [numel, H] rows sorted_token_ids[i] = topk_weights * (a @ w2[e]^T),
+// w = w2 [E, H, K].
+void moe_expert_gemm(Tensor& out, Tensor& a, Tensor& w, Tensor& sorted_token_ids,
+                     Tensor& expert_ids, Tensor& num_tokens_post_pad, int64_t numel,
+                     const c10::optional<Tensor>& topk_weights, int64_t mode,
+                     const c10::optional<Tensor>& fault_flags) {
+  const char* op = "moe_expert_gemm";
+  check_cuda(a, op, "a");
+  for (const Tensor* t : {&out, &w, &sorted_token_ids, &expert_ids, &num_tokens_post_pad})
+    check_same_device(*t, a, op);
+  TORCH_CHECK(mode == 0 || mode == 1, op, ": mode must be 0 (gate/up + SiLU) or 1 (down)");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 || a.scalar_type() == at::kHalf, op,
+              ": a must be bfloat16 or float16");
+  TORCH_CHECK(out.scalar_type() == a.scalar_type() && w.scalar_type() == a.scalar_type(), op,
+              ": out, a and w must share a dtype");
+  for (const Tensor* t : {&sorted_token_ids, &expert_ids, &num_tokens_post_pad})
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->is_contiguous(), op,
+                ": routing tensors must be contiguous int32");
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous(), op, ": w must be a contiguous [E, N, K] tensor");
+  TORCH_CHECK(a.dim() == 2 && out.dim() == 2, op, ": a and out must be 2-D");
+  const Rows ar = rows_of(a, op, "a");
+  const Rows orow = rows_of(out, op, "out");
+  const int64_t E = w.size(0), k = w.size(2);
+  TORCH_CHECK(ar.width == k, op, ": a width ", ar.width, " != w's K ", k);
+  const int64_t n = mode == 0 ? w.size(1) / 2 : w.size(1);
+  TORCH_CHECK(mode == 1 || w.size(1) % 2 == 0, op, ": w1 rows must be 2 * I");
+  TORCH_CHECK(orow.width == n, op, ": out width ", orow.width, " != ", n);
+  TORCH_CHECK(ar.rows <= sorted_token_ids.numel(), op, ": a has more rows than sorted_token_ids");
+  TORCH_CHECK(expert_ids.numel() * 128 >= ar.rows, op,
+              ": expert_ids must hold one entry per 128 sorted rows (moe_align with block 128)");
+  const float* tw = nullptr;
+  if (mode == 0) {
+    TORCH_CHECK(orow.rows >= ar.rows, op, ": out needs a row per sorted row");
+  } else {
+    TORCH_CHECK(topk_weights.has_value(), op, ": mode 1 needs topk_weights");
+    const Tensor& twt = *topk_weights;
+    check_same_device(twt, a, op);
+    TORCH_CHECK(twt.scalar_type() == at::kFloat && twt.is_contiguous() && twt.numel() >= numel,
+                op, ": topk_weights must be a contiguous float32 tensor of >= numel entries");
+    TORCH_CHECK(orow.rows >= numel, op, ": out needs numel rows");
+    tw = twt.data_ptr<float>();
+  }
+  const at::cuda::CUDAGuard guard(a.device());
+  int32_t* fault = counter_ptr(fault_flags, a.device(), op, "fault_flags");
+  check_status(pace_moe_gemm(out.data_ptr(), a.data_ptr(), w.data_ptr(), ar.rows,
+                            sorted_token_ids.data_ptr<int32_t>(), expert_ids.data_ptr<int32_t>(),
+                            num_tokens_post_pad.data_ptr<int32_t>(), numel, tw, (int)E, n, k,
+                            ar.stride, orow.stride, (int)mode, pace_dtype(a), fault,
+                            stream_of(a)),
+               op);
+}
+
 // ------------------------------------------------------------ kv transfer --
 struct CacheSet {
   std::vector<void*> ptrs;
@@ -751,6 +835,17 @@ PYBIND11_MODULE(_C, m) {
           py::arg("topk_ids"), py::arg("num_experts"), py::arg("block_size"),
           py::arg("sorted_token_ids"), py::arg("experts_ids"), py::arg("num_tokens_post_pad"),
           py::arg("fill_padding") = false);
+  moe.def("moe_gather_rows", &moe_gather_rows,
+          "out[i] = input[sorted_token_ids[i] / top_k] (zero rows for padding ids).",
+          py::arg("out"), py::arg("input"), py::arg("sorted_token_ids"),
+          py::arg("num_tokens_post_pad"), py::arg("numel"), py::arg("top_k"));
+  moe.def("moe_expert_gemm", &moe_expert_gemm,
+          "Grouped expert GEMM on the tensor cores: mode 0 gate/up + SiLU-and-mul, mode 1 down "
+          "projection times the routing weight (rows scattered to the token slots).",
+          py::arg("out"), py::arg("a"), py::arg("w"), py::arg("sorted_token_ids"),
+          py::arg("expert_ids"), py::arg("num_tokens_post_pad"), py::arg("numel"),
+          py::arg("topk_weights") = py::none(), py::arg("mode") = 0,
+          py::arg("fault_flags") = py::none());
 
   auto kv = m.def_submodule("kv_transfer_ops");
   kv.def("copy_blocks_p2p", &copy_blocks_p2p,

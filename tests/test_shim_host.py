@@ -79,3 +79,37 @@ def test_install_as_paceserve_registers_modules():
     assert sys.modules["paceserve.layernorm_ops"] is layernorm_ops
     assert sys.modules["paceserve.moe_ops"] is moe_ops
     assert inspect.ismodule(sys.modules["paceserve.activation_ops"])
+
+
+def test_fused_moe_dropin_signatures():
+    """paceserve_b200.fused_moe keeps the parameter names and order of the
+    reference's fused_experts / fused_moe (fused_moe.py:411-425, :547-563)."""
+    from paceserve_b200 import fused_moe as pb_moe
+
+    assert list(inspect.signature(pb_moe.fused_experts).parameters) == [
+        "hidden_states", "w1", "w2", "topk_weights", "topk_ids", "inplace", "override_config",
+        "w1_scale", "w2_scale", "a1_scale", "a2_scale"]
+    assert list(inspect.signature(pb_moe.fused_moe).parameters) == [
+        "hidden_states", "w1", "w2", "gating_output", "topk", "renormalize", "inplace",
+        "override_config", "use_grouped_topk", "num_expert_group", "topk_group", "w1_scale",
+        "w2_scale", "a1_scale", "a2_scale"]
+
+
+def test_new_gemm_ops_present_and_reject_cpu_tensors():
+    assert _params(pos_encoding_ops.qkv_proj_rotary_embedding)[:9] == [
+        "qkv", "hidden", "weight", "positions", "head_size", "num_heads", "num_kv_heads",
+        "cos_sin_cache", "is_neox"]
+    assert _params(moe_ops.moe_expert_gemm)[:9] == [
+        "out", "a", "w", "sorted_token_ids", "expert_ids", "num_tokens_post_pad", "numel",
+        "topk_weights", "mode"]
+    x = torch.zeros(4, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        pos_encoding_ops.qkv_proj_rotary_embedding(torch.empty(4, 512, dtype=torch.bfloat16), x,
+                                                   torch.zeros(512, 64, dtype=torch.bfloat16),
+                                                   torch.zeros(4, dtype=torch.long), 128, 2, 1,
+                                                   torch.zeros(16, 128), True)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        moe_ops.moe_expert_gemm(x, x, torch.zeros(2, 256, 64, dtype=torch.bfloat16),
+                                torch.zeros(128, dtype=torch.int32),
+                                torch.zeros(1, dtype=torch.int32),
+                                torch.zeros(1, dtype=torch.int32), 4, None, 0)
