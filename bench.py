@@ -1206,11 +1206,28 @@ def qkv_rope_bench(dev, tokens=(1, 128, 512, 2048), reps=10):
         res["tflops"] = round(flops / (res["fused_us"] * 1e-6) / 1e12, 1)
         res["frac_of_bf16_peak"] = round(res["tflops"] / peak["bf16_tflops"], 4)
         res["speedup_vs_unfused"] = round(res["cublas_gemm_plus_rope_us"] / res["fused_us"], 3)
+        # roofline: the larger of tensor time and the time to move the weight,
+        # the hidden rows and the output once
+        nbytes = 2.0 * (n * H + t * H + t * n)
+        t_roof_us = max(flops / (peak["bf16_tflops"] * 1e12), nbytes / (peak["hbm_gbs"] * 1e9)) * 1e6
+        res["roofline_us"] = round(t_roof_us, 2)
+        res["frac_of_roofline"] = round(t_roof_us / res["fused_us"], 4)
         res["rel_err_vs_unfused"] = round(err, 5)
         rows.append(res)
         del xs, outs, refs
         torch.cuda.empty_cache()
     return rows
+
+
+def _vllm_fused_experts():
+    """vLLM's fused_experts (the library version of the reference's Triton
+    fused MoE) as a baseline, or the reason it cannot run."""
+    try:
+        from vllm.model_executor.layers.fused_moe.fused_moe import fused_experts
+
+        return fused_experts
+    except Exception as exc:  # reported in the line, never fatal
+        return f"{type(exc).__name__}: {exc}"[:200]
 
 
 def moe_experts_bench(dev, tokens=(64, 512, 4096), reps=5):
@@ -1258,10 +1275,24 @@ def moe_experts_bench(dev, tokens=(64, 512, 4096), reps=5):
                 out.index_add_(0, tok, y)
             return out.bfloat16()
 
+        variants = [("fused_experts_us", ours), ("cublas_per_expert_us", per_expert)]
+        vllm_fn = _vllm_fused_experts()
+        if callable(vllm_fn):
+            variants.append(("vllm_fused_experts_us", lambda: vllm_fn(x, w1, w2, tw, ids)))
         res = {"T": t}
-        for name, fn in (("fused_experts_us", ours), ("cublas_per_expert_us", per_expert)):
-            fn()
-            torch.cuda.synchronize()
+        if not callable(vllm_fn):
+            res["vllm_fused_experts_us"] = None
+            res["vllm_unavailable"] = vllm_fn
+        for name, fn in variants:
+            try:
+                fn()
+                torch.cuda.synchronize()
+            except Exception as exc:  # only the baseline can fail here
+                if name == "fused_experts_us":
+                    raise
+                res[name] = None
+                res["vllm_unavailable"] = f"{type(exc).__name__}: {exc}"[:200]
+                continue
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(reps):
@@ -1275,9 +1306,48 @@ def moe_experts_bench(dev, tokens=(64, 512, 4096), reps=5):
         res["tflops"] = round(flops / (res["fused_experts_us"] * 1e-6) / 1e12, 1)
         res["frac_of_bf16_peak"] = round(res["tflops"] / peak["bf16_tflops"], 4)
         res["speedup_vs_per_expert"] = round(res["cublas_per_expert_us"] / res["fused_experts_us"], 3)
+        if res.get("vllm_fused_experts_us"):
+            res["speedup_vs_vllm"] = round(res["vllm_fused_experts_us"] / res["fused_experts_us"], 3)
+        # roofline: the larger of tensor time and the time to read the experts'
+        # weights once (the layer is weight-bound at small T)
+        wbytes = 2.0 * (w1.numel() + w2.numel())
+        t_roof_us = max(flops / (peak["bf16_tflops"] * 1e12), wbytes / (peak["hbm_gbs"] * 1e9)) * 1e6
+        res["roofline_us"] = round(t_roof_us, 1)
+        res["frac_of_roofline"] = round(t_roof_us / res["fused_experts_us"], 4)
         res["rel_err_vs_per_expert"] = round(((a - b).abs().max() / b.abs().max()).item(), 5)
         rows.append(res)
     return rows
+
+
+def tc_calls(dev, tokens: int, calls: int):
+    """`calls` eager calls each of the fused qkv projection + rope (Llama-3-8B,
+    4096 -> 6144) and of fused_moe (Mixtral-8x7B, E=8, top-2) at `tokens`
+    tokens: the launches an ncu capture of the tensor-core kernels selects
+    from.  Returns the calls' mean wall time (not a bench figure)."""
+    import torch
+
+    import paceserve_b200 as pb
+    from paceserve_b200 import fused_moe as pb_moe
+
+    g_ = torch.Generator(device=dev).manual_seed(3)
+    n = (NQ + 2 * NKV) * HD
+    w = (torch.randn(n, H, generator=g_, device=dev) / H ** 0.5).bfloat16()
+    x = torch.randn(tokens, H, generator=g_, device=dev).bfloat16()
+    pos = torch.randint(0, MAX_POS, (tokens,), generator=g_, device=dev)
+    cache = rope_cache(dev)
+    qkv = torch.empty(tokens, n, dtype=torch.bfloat16, device=dev)
+    E, k, inter = 8, 2, 14336
+    w1 = (torch.randn(E, 2 * inter, H, generator=g_, device=dev) / H ** 0.5).bfloat16()
+    w2 = (torch.randn(E, H, inter, generator=g_, device=dev) / inter ** 0.5).bfloat16()
+    gating = torch.randn(tokens, E, generator=g_, device=dev)
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        pb.pos_encoding_ops.qkv_proj_rotary_embedding(qkv, x, w, pos, HD, NQ, NKV, cache, True)
+        out = pb_moe.fused_moe(x, w1, w2, gating, k, True)
+    torch.cuda.synchronize()
+    return {"tokens": tokens, "calls": calls,
+            "wall_ms_per_call_pair": round((time.perf_counter() - t0) * 1e3 / calls, 3),
+            "checksum": round(float(out.float().abs().mean()), 5)}
 
 
 # ------------------------------------------------------------------ main --
@@ -1372,6 +1442,10 @@ def run_side_workload(args, ws, rank, local):
     elif args.workload == "sweep":
         line = {"metric": "per-op HBM GB/s, token sweep", "sweep": sweep(dev) if rank == 0 else None,
                 "peak_gbs": peaks()["hbm_gbs"]}
+    elif args.workload == "tc":
+        line = {"metric": "tensor-core ops: fused qkv projection + rope and the MoE expert "
+                          "layer, eager calls (for ncu captures)",
+                "tc": tc_calls(dev, args.tokens, args.steps)}
     else:
         line = {"metric": "MoE routing us/op", "moe": moe_routing(dev) if rank == 0 else None}
     if ws > 1:
@@ -1395,12 +1469,15 @@ def main():
                     help="skip the config-3 sweep and config-4 MoE keys of the N=1 line")
     ap.add_argument("--kv-blocks", type=int, default=8192,
                     help="blocks per layer of the kv workload's caches (a smaller case for ncu)")
-    ap.add_argument("--workload", choices=["chain", "kv", "sweep", "moe", "opgraph"],
+    ap.add_argument("--workload", choices=["chain", "kv", "sweep", "moe", "opgraph", "tc"],
                     default="chain",
                     help="chain: the headline op chain (the driver's line); kv: LP->HP "
                          "promotion; sweep: per-op token sweep; moe: Mixtral-8x7B routing; "
                          "opgraph: one op's launches over distinct layer buffers, as a CUDA "
-                         "graph (for ncu captures)")
+                         "graph (for ncu captures); tc: --steps eager calls of the fused qkv "
+                         "projection + rope (Llama-3-8B) and of fused_moe (Mixtral-8x7B) at "
+                         "--tokens tokens (for ncu captures)")
+    ap.add_argument("--tokens", type=int, default=512, help="tc: tokens per call")
     ap.add_argument("--layers", type=int, default=32,
                     help="opgraph: launches (layers) per graph")
     ap.add_argument("--op", default="silu_and_mul",
