@@ -1432,8 +1432,12 @@ def run_side_workload(args, ws, rank, local):
         with torch.cuda.graph(gr, stream=s_):
             for b in layers:
                 one[0](b)
+        # the replays sit in an NVTX range, so a graph-level ncu capture can
+        # select them (ncu --graph-profiling graph --nvtx --nvtx-include opgraph_replays/)
+        torch.cuda.nvtx.range_push("opgraph_replays")
         for _ in range(args.steps):
             gr.replay()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         line = {"metric": f"{args.op} graph replays (T=512 Sarathi batch, Llama-3-8B shapes) "
                           "for ncu captures",

@@ -25,8 +25,8 @@
 // 4-stage TMA ring (128-byte swizzle, no multicast), tcgen05.mma M=128 N=256
 // into one of two TMEM accumulators, 8 epilogue warps; one persistent CTA per
 // SM walks the tiles round-robin, m blocks fastest so that CTAs running
-// together share an expert's weight tile in L2.  Blocks at or past
-// num_tokens_post_pad / 128 are skipped.  Every mbarrier wait is bounded.
+// together share an expert's weight tile in L2.  Only blocks below
+// num_tokens_post_pad / 128 are walked.  Every mbarrier wait is bounded.
 #include "tcgen05.cuh"
 
 namespace pace {
@@ -83,19 +83,18 @@ __device__ __forceinline__ void store16(T* p, const float* v) {
 // silu(x) = x / (1 + e^-x) in fp32 (csrc/activation_kernels.cu:8-12).
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
-// The tiles this CTA owns, in order: t = cta, cta + grid, ... over
-// m_blocks x n_tiles (m fastest), skipping blocks past the padded total.
+// The tiles this CTA owns, in order: t = cta, cta + grid, ... over the
+// valid_blocks x n_tiles tiles that hold routed rows (m fastest).  Only the
+// blocks below the padded total (read on the device) are walked, so every CTA
+// gets the same number of tiles, give or take one.
 struct TileWalk {
-  int t, step, m_blocks, n_tiles, valid_blocks;
+  int t, step, n_tiles, valid_blocks;
   __device__ __forceinline__ bool next(int& mb, int& nt) {
-    while (t < m_blocks * n_tiles) {
-      const int cur = t;
-      t += step;
-      mb = cur % m_blocks;
-      nt = cur / m_blocks;
-      if (mb < valid_blocks) return true;
-    }
-    return false;
+    if (t >= valid_blocks * n_tiles) return false;
+    mb = t % valid_blocks;
+    nt = t / valid_blocks;
+    t += step;
+    return true;
   }
 };
 
@@ -149,7 +148,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == EPI_WARPS) {
     // ---- TMA producer ----------------------------------------------------
     if (lane == 0) {
-      TileWalk walk{(int)blockIdx.x, (int)gridDim.x, m_blocks, n_tiles, valid_blocks};
+      TileWalk walk{(int)blockIdx.x, (int)gridDim.x, n_tiles, valid_blocks};
       int64_t i = 0;
       bool ok = true;
       int mb, nt;
@@ -187,7 +186,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
       constexpr uint32_t idesc = tc::umma_idesc_f16(kBf16, BM, BN);
-      TileWalk walk{(int)blockIdx.x, (int)gridDim.x, m_blocks, n_tiles, valid_blocks};
+      TileWalk walk{(int)blockIdx.x, (int)gridDim.x, n_tiles, valid_blocks};
       int64_t i = 0;
       int j = 0;
       bool ok = true;
@@ -229,7 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- epilogue: warp w drains TMEM lanes 32 (w % 4) .. +31 -------------
     const int quarter = warp % 4, half = warp / 4;
     const int row = quarter * 32 + lane;
-    TileWalk walk{(int)blockIdx.x, (int)gridDim.x, m_blocks, n_tiles, valid_blocks};
+    TileWalk walk{(int)blockIdx.x, (int)gridDim.x, n_tiles, valid_blocks};
     int j = 0;
     int mb, nt;
     while (walk.next(mb, nt)) {
