@@ -1529,6 +1529,8 @@ def main():
             "frac": round(silu["gbs"] / pk["hbm_gbs"], 4), "peak_source": pk["source"],
             "frac_of_nominal": round(silu["gbs"] / NOMINAL_HBM_GBS, 4),
             "traffic": ncu_traffic("silu_and_mul_T512"),
+            "traffic_source": "DRAM read + write per launch from an ncu capture of the whole "
+                              "32-launch graph (write-backs included), profiles/ncu_traffic.txt",
             "algorithmic_bytes": B_SILU}
     chs = [ch, build_chain(dev, seed=4321 + rank)]
     e2e = e2e_chain(chs, ops, steps=min(args.steps, 50), warmup=3, ws=ws)
