@@ -1219,6 +1219,75 @@ def qkv_rope_bench(dev, tokens=(1, 128, 512, 2048), reps=10):
     return rows
 
 
+def norm_gemm_bench(dev, tokens=(512, 2048), reps=10):
+    """The layer boundary o_proj -> residual add -> input RMSNorm -> qkv_proj
+    -> rope (Llama-3-8B, bf16) fused into two tensor-core GEMMs
+    (linear_residual with the residual add and the norm's sum-of-squares
+    partials in its epilogue; qkv_proj_rmsnorm_rotary_embedding with the norm
+    factor and rope in its epilogue) against the unfused path: cuBLAS o_proj,
+    this package's fused_add_rms_norm, cuBLAS qkv_proj and rotary_embedding.
+    CUDA graphs over 3 weight sets (> L2); outputs compared within the bf16
+    rule."""
+    import torch
+
+    import paceserve_b200 as pb
+
+    nbuf = 3
+    n = (NQ + 2 * NKV) * HD
+    g_ = torch.Generator(device=dev).manual_seed(21)
+    w_o = [(torch.randn(H, H, generator=g_, device=dev) / H ** 0.5).bfloat16() for _ in range(nbuf)]
+    w_qkv = [(torch.randn(n, H, generator=g_, device=dev) / H ** 0.5).bfloat16() for _ in range(nbuf)]
+    w_norm = [(torch.randn(H, generator=g_, device=dev) * 0.02 + 1).bfloat16() for _ in range(nbuf)]
+    folded = [pb.fold_rmsnorm_weight(w, nw) for w, nw in zip(w_qkv, w_norm)]
+    cache = rope_cache(dev)
+    rows = []
+    for t in tokens:
+        attn = [torch.randn(t, H, generator=g_, device=dev).bfloat16() for _ in range(nbuf)]
+        res0 = [torch.randn(t, H, generator=g_, device=dev).bfloat16() for _ in range(nbuf)]
+        pos = torch.randint(0, MAX_POS, (t,), generator=g_, device=dev)
+        res_f = [r.clone() for r in res0]
+        res_u = [r.clone() for r in res0]
+        ss = [torch.empty(t, H // 32, device=dev) for _ in range(nbuf)]
+        qkv_f = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        qkv_u = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        xo = [torch.empty(t, H, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+
+        def fused():
+            for i in range(nbuf):
+                pb.layernorm_ops.linear_residual(res_f[i], attn[i], w_o[i], ss[i])
+                pb.pos_encoding_ops.qkv_proj_rmsnorm_rotary_embedding(
+                    qkv_f[i], res_f[i], folded[i], ss[i], EPS, pos, HD, NQ, NKV, cache, True)
+
+        def unfused():
+            for i in range(nbuf):
+                torch.matmul(attn[i], w_o[i].t(), out=xo[i])
+                pb.layernorm_ops.fused_add_rms_norm(xo[i], res_u[i], w_norm[i], EPS)
+                torch.matmul(xo[i], w_qkv[i].t(), out=qkv_u[i])
+                q = qkv_u[i]
+                pb.pos_encoding_ops.rotary_embedding(pos, q[:, : NQ * HD],
+                                                     q[:, NQ * HD: (NQ + NKV) * HD], HD, cache,
+                                                     True)
+
+        res = {"T": t}
+        for name, fn, resets in (("fused_us", fused, res_f), ("unfused_us", unfused, res_u)):
+            fn()  # eager once (workspace allocation outside capture)
+            gr = capture(fn)
+            res[name] = round(time_replays(gr, reps, 3) * 1e3 / (reps * nbuf), 3)
+            del gr
+            for r_, r0 in zip(resets, res0):  # the residual accumulated over replays
+                r_.copy_(r0)
+        fused()
+        unfused()
+        torch.cuda.synchronize()
+        qf, qu = qkv_f[0].float(), qkv_u[0].float()
+        res["speedup_vs_unfused"] = round(res["unfused_us"] / res["fused_us"], 3)
+        res["rel_err_qkv"] = round(((qf - qu).abs().max() / qu.abs().max()).item(), 5)
+        rows.append(res)
+        del attn, res0, res_f, res_u, ss, qkv_f, qkv_u, xo
+        torch.cuda.empty_cache()
+    return rows
+
+
 def _vllm_fused_experts():
     """vLLM's fused_experts (the library version of the reference's Triton
     fused MoE) as a baseline, or the reason it cannot run."""
@@ -1577,6 +1646,12 @@ def main():
                                     "the epilogue) vs cuBLAS GEMM then the rope op; Llama-3-8B "
                                     "4096 -> 6144, bf16, 4 weight buffers per graph (> L2)",
                             "peak_tflops": pk["bf16_tflops"], "rows": qkv_rope_bench(dev)}
+        torch.cuda.empty_cache()
+        line["norm_gemm"] = {"what": "o_proj + residual add + input RMSNorm + qkv_proj + rope "
+                                     "(Llama-3-8B, bf16) as two tensor-core GEMMs with the add, "
+                                     "the norm and rope in their epilogues, vs cuBLAS + this "
+                                     "package's fused_add_rms_norm and rope",
+                             "rows": norm_gemm_bench(dev)}
         torch.cuda.empty_cache()
         line["moe_experts"] = {"what": "Mixtral-8x7B expert layer (E=8, top-2, 4096 -> 14336 -> "
                                        "4096, bf16): fused_experts on tcgen05 grouped GEMMs vs "

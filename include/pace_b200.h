@@ -120,6 +120,46 @@ int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
                        int64_t max_position, int is_neox, int dtype, void* workspace,
                        size_t workspace_bytes, int32_t* fault_flags, cudaStream_t stream);
 
+/* ---- RMSNorm folded into the GEMMs around it ----------------------------
+ * The decoder layer's "residual + x, then RMSNorm" (fused_add_rms_norm; in the
+ * reference the add and RMSNorm.forward at paceserve/model_executor/models/
+ * llama.py:240-254) split over the GEMMs that produce and consume it:
+ *
+ * pace_linear_residual: residual[t, :n] = (T)(residual[t] + input[t] @ weight^T)
+ *   (o_proj / down_proj with the residual add in the epilogue; weight
+ *   [n, k] row-major, n % 128 == 0), and, when row_sumsq is not NULL,
+ *   row_sumsq[t, g] = sum of the new residual's squares over columns
+ *   [32g, 32g + 32) (fp32, [T, n / 32]).  Workspace as for
+ *   pace_qkv_proj_rope (pace_linear_residual_workspace_size; zero-filled
+ *   before first use, left valid by every call).
+ * pace_row_sumsq: the same partials for rows no GEMM produced (layer 0).
+ * pace_qkv_proj_rmsnorm_rope: pace_qkv_proj_rope on un-normalised rows
+ *   `hidden`, with the RMSNorm applied as a per-row factor in the epilogue:
+ *   qkv = rope(inv[t] * (hidden[t] @ folded_weight^T)),
+ *   inv[t] = rsqrt(sum_g row_sumsq[t, g] / hidden_size + epsilon), where
+ *   folded_weight[n, c] = (T)(w_qkv[n, c] * norm_weight[c]) is prepared once by
+ *   the caller.  Equal to rms_norm then the projection up to the rounding of
+ *   the normalised rows (the reference rounds them to T before its GEMM).
+ *   row_sumsq 16-byte aligned, sumsq_groups (= hidden_size / 32) a multiple
+ *   of 4.
+ * Replace fused_add_rms_norm + qkv_proj (llama.py:176, 240-254) and the
+ * residual add after o_proj / the MLP.  No reference kernel. */
+size_t pace_linear_residual_workspace_size(int64_t num_tokens, int64_t n, int64_t k, int device);
+int pace_linear_residual(void* residual, const void* input, const void* weight, float* row_sumsq,
+                         int64_t num_tokens, int64_t n, int64_t k, int64_t input_row_stride,
+                         int64_t residual_row_stride, int dtype, void* workspace,
+                         size_t workspace_bytes, int32_t* fault_flags, cudaStream_t stream);
+int pace_row_sumsq(float* row_sumsq, const void* input, int64_t num_tokens, int64_t hidden_size,
+                   int64_t input_row_stride, int dtype, cudaStream_t stream);
+int pace_qkv_proj_rmsnorm_rope(void* qkv_out, const void* hidden, const void* folded_weight,
+                               const float* row_sumsq, int64_t sumsq_groups, float epsilon,
+                               const int64_t* positions, int64_t num_tokens,
+                               int64_t hidden_size, int num_heads, int num_kv_heads,
+                               int head_size, int64_t hidden_row_stride, int64_t out_row_stride,
+                               const void* cos_sin_cache, int cache_dtype, int rot_dim,
+                               int64_t max_position, int is_neox, int dtype, void* workspace,
+                               size_t workspace_bytes, int32_t* fault_flags, cudaStream_t stream);
+
 /* Allocation-free variant of pace_qkv_proj_rope.  No counterpart in the
  * reference.  For callers that cannot allocate device memory: a plugin host
  * that hands an op only its input and output buffers, or a latency-bound

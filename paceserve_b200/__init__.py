@@ -51,6 +51,15 @@ def get_pdl() -> bool:
     return bool(_C.get_pdl())
 
 
+def fold_rmsnorm_weight(linear_weight, norm_weight):
+    """The projection weight with an RMSNorm weight folded into its input
+    columns, W'[n, c] = W[n, c] * w[c] (rounded to W's dtype), for the GEMMs
+    that apply the norm as a per-row factor in their epilogue
+    (``pos_encoding_ops.qkv_proj_rmsnorm_rotary_embedding``).  Prepared once per
+    model load."""
+    return (linear_weight.float() * norm_weight.float()[None, :]).to(linear_weight.dtype).contiguous()
+
+
 def install_as_paceserve() -> None:
     """Register these modules as ``paceserve.{layernorm,pos_encoding,activation,moe}_ops``.
 
@@ -81,6 +90,7 @@ __all__ = [
     "moe_ops",
     "kv_transfer_ops",
     "install_as_paceserve",
+    "fold_rmsnorm_weight",
     "set_pdl",
     "get_pdl",
     "LIBRARY_PATH",

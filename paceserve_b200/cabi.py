@@ -59,6 +59,18 @@ SIGNATURES: dict[str, tuple] = {
          c_int, c_int64, c_int, c_int, _P, c_size_t, _P, _P],
     ),
     "pace_qkv_proj_rope_workspace_size": (c_size_t, [c_int64, c_int64, c_int, c_int, c_int]),
+    "pace_linear_residual_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int]),
+    "pace_linear_residual": (
+        c_int,
+        [_P, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, _P, c_size_t, _P,
+         _P],
+    ),
+    "pace_row_sumsq": (c_int, [_P, _P, c_int64, c_int64, c_int64, c_int, _P]),
+    "pace_qkv_proj_rmsnorm_rope": (
+        c_int,
+        [_P, _P, _P, _P, c_int64, c_float, _P, c_int64, c_int64, c_int, c_int, c_int, c_int64,
+         c_int64, _P, c_int, c_int, c_int64, c_int, c_int, _P, c_size_t, _P, _P],
+    ),
     "pace_moe_gather_rows": (
         c_int, [_P, _P, _P, c_int64, _P, c_int64, c_int, c_int64, c_int64, c_int64, c_int, _P]),
     "pace_moe_gemm": (

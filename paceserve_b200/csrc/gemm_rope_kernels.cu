@@ -168,17 +168,43 @@ __device__ __forceinline__ float* slot_q(float* slot, int chunk, int q, int row)
 }
 
 // ---- epilogue ------------------------------------------------------------
-// A thread finishes 16-column pieces of one tile row of one head:
-//   NeoX : step i (0..3) holds x = head cols [16i, 16i+16) and
-//          y = [64+16i, 64+16i+16), rotated with cache entries 16i .. 16i+15;
-//   GPT-J: step i holds a = head cols [32i, 32i+16) and b = [32i+16, 32i+32),
-//          pairs (2p, 2p+1) rotated with cache entries 16i + p.
-// cs: the token's cache row, or null when the head is not rotated (v heads,
-// rows past the end, positions outside the cache).
-template <bool NEOX>
-__device__ __forceinline__ int col_a(int i) { return NEOX ? 16 * i : 32 * i; }
-template <bool NEOX>
-__device__ __forceinline__ int col_b(int i) { return NEOX ? 64 + 16 * i : 32 * i + 16; }
+// Epilogue kinds: the rotary embedding of the q/k heads (NeoX or GPT-J
+// pairs), or the residual add of o_proj / down_proj.  NORM (rope kinds):
+// each row of the accumulator is first scaled by its RMSNorm factor
+// inv = rsqrt(sum of the row's squares / K + eps), from the sum-of-squares
+// partials the producer of the input rows wrote (the residual epilogue, or
+// pace_row_sumsq); the norm weight is folded into the GEMM weight by the
+// caller, so x_norm @ W^T = inv * (h @ (W diag(w))^T).
+constexpr int EPI_ROPE_NEOX = 0, EPI_ROPE_GPTJ = 1, EPI_RESIDUAL = 2;
+constexpr int SUMSQ_GROUP = 32;  // columns per sum-of-squares partial
+
+struct EpiParams {
+  // rope
+  const int64_t* positions;
+  const void* cache;
+  int64_t max_position;
+  int rot_heads, total_heads;
+  // NORM: the input rows' sum-of-squares partials [rows, sumsq_in_groups]
+  const float* sumsq_in;
+  int sumsq_in_groups;
+  float inv_k, eps;
+  // residual: partials of the new residual rows [rows, n_cols / 32], or null
+  float* sumsq_out;
+  int n_cols;  // output columns (rope: total_heads * 128)
+};
+
+// A thread finishes 16-column pieces of one tile row of one 128-column group
+// ("head"): step i (0..3) holds a at head column col_a(i) and b at col_b(i).
+//   NeoX : a = x = [16i, 16i+16), b = y = [64+16i, +16), cache entries 16i + e;
+//   GPT-J: a = [32i, 32i+16), b = [32i+16, 32i+32), pairs (2p, 2p+1) with cache
+//          entries 16i + p;
+//   residual: the same columns as GPT-J; step i is sum-of-squares group 4h + i.
+template <int EPI>
+__device__ __forceinline__ int col_a(int i) { return EPI == EPI_ROPE_NEOX ? 16 * i : 32 * i; }
+template <int EPI>
+__device__ __forceinline__ int col_b(int i) {
+  return EPI == EPI_ROPE_NEOX ? 64 + 16 * i : 32 * i + 16;
+}
 
 template <typename C>
 __device__ __forceinline__ void load_step_cs(const C* cs, int i, float* cv, float* sv) {
@@ -186,9 +212,9 @@ __device__ __forceinline__ void load_step_cs(const C* cs, int i, float* cv, floa
   load_cs<C, 16>(cs + HEAD / 2 + 16 * i, sv);
 }
 
-template <bool NEOX>
+template <int EPI>
 __device__ __forceinline__ void rotate(float* a, float* b, const float* cv, const float* sv) {
-  if (NEOX) {
+  if (EPI == EPI_ROPE_NEOX) {
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const float x = a[e], y = b[e];
@@ -208,29 +234,101 @@ __device__ __forceinline__ void rotate(float* a, float* b, const float* cv, cons
   }
 }
 
-// Cache row of the token in row m for a head, or null (see above).
+template <typename T>
+__device__ __forceinline__ void load16(const T* p, float* v) {
+  Traits<T>::unpack(ld_v4(p), v);
+  Traits<T>::unpack(ld_v4(p + 8), v + 8);
+}
+
+// What one thread needs to finish its head of one tile row.
 template <typename C>
-__device__ __forceinline__ const C* cache_row(const C* cache, const int64_t* positions,
-                                              int64_t max_position, int m, bool valid,
-                                              bool rotated_head) {
-  if (!valid || !rotated_head) return nullptr;
-  const int64_t pos = positions[m];
-  return pos >= 0 && pos < max_position ? cache + pos * HEAD : nullptr;
+struct RowState {
+  const C* cs;  // rope: the token's cache row, or null (not rotated)
+  float inv;    // NORM factor (1 without NORM)
+  bool store;   // the row exists and the head is inside the output
+};
+
+// Row state of row m, 128-column group `head` (global index).  NORM: the
+// partials are added in group order, so every thread of a row derives the
+// same factor.
+template <typename C, int EPI, bool NORM>
+__device__ __forceinline__ RowState<C> row_state(const EpiParams& ep, int m, bool valid,
+                                                 int head) {
+  RowState<C> s;
+  s.cs = nullptr;
+  s.inv = 1.f;
+  s.store = valid && (EPI == EPI_RESIDUAL ? head * HEAD < ep.n_cols : head < ep.total_heads);
+  if (EPI != EPI_RESIDUAL && valid && head < ep.rot_heads) {
+    const int64_t pos = ep.positions[m];
+    if (pos >= 0 && pos < ep.max_position)
+      s.cs = static_cast<const C*>(ep.cache) + pos * HEAD;
+  }
+  if (NORM && valid) {
+    const float* p = ep.sumsq_in + (int64_t)m * ep.sumsq_in_groups;
+    float ss = 0.f;
+    int g = 0;
+    for (; g + 4 <= ep.sumsq_in_groups; g += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p + g));
+      ss += v.x;
+      ss += v.y;
+      ss += v.z;
+      ss += v.w;
+    }
+    for (; g < ep.sumsq_in_groups; ++g) ss += __ldg(p + g);
+    s.inv = rsqrtf(ss * ep.inv_k + ep.eps);
+  }
+  return s;
+}
+
+// Step i of a row: a (at col_a) and b (at col_b) hold the fp32 accumulator;
+// o is the row's output at the head's first column.  Returns the step's sum
+// of squares (residual), else 0.
+template <typename T, typename C, int EPI, bool NORM>
+__device__ __forceinline__ float apply_step(const RowState<C>& s, int i, float* a, float* b,
+                                            T* o) {
+  if (NORM) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      a[e] *= s.inv;
+      b[e] *= s.inv;
+    }
+  }
+  float ss = 0.f;
+  if (EPI == EPI_RESIDUAL) {
+    if (s.store) {
+      float ra[16], rb[16];
+      load16(o + col_a<EPI>(i), ra);
+      load16(o + col_b<EPI>(i), rb);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        a[e] = Traits<T>::round(a[e] + ra[e]);
+        b[e] = Traits<T>::round(b[e] + rb[e]);
+        ss += a[e] * a[e] + b[e] * b[e];
+      }
+    }
+  } else if (s.cs) {
+    float cv[16], sv[16];
+    load_step_cs(s.cs, i, cv, sv);
+    rotate<EPI>(a, b, cv, sv);
+  }
+  if (s.store) {
+    store16(o + col_a<EPI>(i), a);
+    store16(o + col_b<EPI>(i), b);
+  }
+  return ss;
 }
 
 // A whole tile from TMEM: this thread's row, one head (128 columns at TMEM
 // address `taddr`).  All lanes of the warp call it (TMEM loads are
-// warp-wide); `store` is false for rows past the end and absent heads.  Each
-// step's cos/sin loads are issued before its TMEM loads, so the two overlap.
-template <typename T, typename C, bool NEOX>
-__device__ __forceinline__ void finish_head_tmem(uint32_t taddr, T* o, const C* cs, bool store) {
+// warp-wide).  ss_out: the row's sum-of-squares partials (residual), or null.
+template <typename T, typename C, int EPI, bool NORM>
+__device__ __forceinline__ void finish_head_tmem(uint32_t taddr, T* o, const RowState<C>& s,
+                                                 float* ss_out, int head) {
 #pragma unroll 1
   for (int i = 0; i < 4; ++i) {
-    float cv[16], sv[16];
-    if (cs) load_step_cs(cs, i, cv, sv);
     uint32_t ra[16], rb[16];
-    tc::tmem_ld16(taddr + col_a<NEOX>(i), ra);
-    tc::tmem_ld16(taddr + col_b<NEOX>(i), rb);
+    tc::tmem_ld16(taddr + col_a<EPI>(i), ra);
+    tc::tmem_ld16(taddr + col_b<EPI>(i), rb);
     tc::tmem_wait_ld(ra);
     tc::tmem_wait_ld(rb);
     float a[16], b[16];
@@ -239,11 +337,8 @@ __device__ __forceinline__ void finish_head_tmem(uint32_t taddr, T* o, const C* 
       a[e] = __uint_as_float(ra[e]);
       b[e] = __uint_as_float(rb[e]);
     }
-    if (cs) rotate<NEOX>(a, b, cv, sv);
-    if (store) {
-      store16(o + col_a<NEOX>(i), a);
-      store16(o + col_b<NEOX>(i), b);
-    }
+    const float ss = apply_step<T, C, EPI, NORM>(s, i, a, b, o);
+    if (EPI == EPI_RESIDUAL && ss_out && s.store) ss_out[head * 4 + i] = ss;
   }
 }
 
@@ -289,65 +384,54 @@ __device__ __forceinline__ void add16(float* v, const float* slot, int chunk, in
 // epilogue warps split it by column: warp w takes step w % 4 of head w / 4
 // for every valid row (lane + 32 p), so each load of a warp reads 32
 // consecutive rows of one chunk.  Partials are added in segment order.
-template <typename T, typename C, bool NEOX>
+template <typename T, typename C, int EPI, bool NORM>
 __device__ __forceinline__ void fixup_tile(const float* slots, const Split& sp, int64_t tile_u0,
                                            int c0, int c1, T* out_tile, int64_t out_stride,
-                                           const C* cache, const int64_t* positions,
-                                           int64_t max_position, int m0, int valid_rows,
-                                           int head0, int rot_heads, int total_heads, int warp,
-                                           int lane) {
+                                           const EpiParams& ep, int m0, int valid_rows,
+                                           int head0, int warp, int lane) {
   const int hh = warp / 4, i = warp % 4;
   const int head = head0 + hh;
-  if (head >= total_heads) return;
-  const bool rotated = head < rot_heads;
-  const int ca = hh * 8 + col_a<NEOX>(i) / 16, cb = hh * 8 + col_b<NEOX>(i) / 16;
-  // the four rows' positions first, so their loads overlap
-  const C* rows_cs[BM / 32];
-#pragma unroll
-  for (int p = 0; p < BM / 32; ++p) {
-    const int r = lane + 32 * p;
-    rows_cs[p] = cache_row(cache, positions, max_position, m0 + r, r < valid_rows, rotated);
-  }
-#pragma unroll
+  const int ca = hh * 8 + col_a<EPI>(i) / 16, cb = hh * 8 + col_b<EPI>(i) / 16;
+  const int groups = ep.n_cols / SUMSQ_GROUP;
+#pragma unroll 1
   for (int p = 0; p < BM / 32; ++p) {
     const int r = lane + 32 * p;
     if (r >= valid_rows) break;
-    const C* cs = rows_cs[p];
-    float a[16], b[16], cv[16], sv[16];
+    const RowState<C> s = row_state<C, EPI, NORM>(ep, m0 + r, true, head);
+    if (!s.store) break;  // the head is past the output (odd head counts)
+    float a[16], b[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
-    if (cs) load_step_cs(cs, i, cv, sv);
 #pragma unroll 2
     for (int c = c0; c <= c1; ++c) {
       const int slot = sp.start(c) >= tile_u0 ? 2 * c : 2 * c + 1;
-      const float* s = slots + (int64_t)slot * SLOT_FLOATS;
-      add16(a, s, ca, r);
-      add16(b, s, cb, r);
+      const float* sl = slots + (int64_t)slot * SLOT_FLOATS;
+      add16(a, sl, ca, r);
+      add16(b, sl, cb, r);
     }
-    if (cs) rotate<NEOX>(a, b, cv, sv);
     T* o = out_tile + (int64_t)r * out_stride + hh * HEAD;
-    store16(o + col_a<NEOX>(i), a);
-    store16(o + col_b<NEOX>(i), b);
+    const float ss = apply_step<T, C, EPI, NORM>(s, i, a, b, o);
+    if (EPI == EPI_RESIDUAL && ep.sumsq_out)
+      ep.sumsq_out[(int64_t)(m0 + r) * groups + head * 4 + i] = ss;
   }
 }
 
 // One persistent CTA per SM (grid = min(SMs, units)); see the file comment.
 // slots: 2 partial tiles of BM x BN floats per CTA; counters: one int32 per
 // tile, zero before the call and left zero by it.
-template <typename T, typename C, bool NEOX>
+template <typename T, typename C, int EPI, bool NORM>
 __global__ void __launch_bounds__(THREADS, 1)
-    qkv_rope_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                    T* __restrict__ out, int64_t out_stride, const int64_t* __restrict__ positions,
-                    const C* __restrict__ cache, int64_t max_position, int num_tokens,
-                    int m_tiles, int k_blocks, int rot_heads, int total_heads,
-                    int* __restrict__ counters, float* __restrict__ slots, int32_t* fault) {
+    gemm_epi_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                    T* __restrict__ out, int64_t out_stride, int num_tokens, int m_tiles,
+                    int k_blocks, const EpiParams ep, int* __restrict__ counters,
+                    float* __restrict__ slots, int32_t* fault) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   Ctl* ctl = reinterpret_cast<Ctl*>(tiles + STAGES * STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
-  const int n_tiles = (total_heads * HEAD + BN - 1) / BN;
+  const int n_tiles = (ep.n_cols + BN - 1) / BN;
   const int64_t n_all = (int64_t)m_tiles * n_tiles;
   const int64_t t_stop = n_all / gridDim.x * gridDim.x;  // first stream-K tile
   Split sp;  // stream-K split of the units of tiles [t_stop, n_all)
@@ -475,9 +559,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool valid = m < num_tokens;
       const int head = nt * (BN / HEAD) + hh;
       const bool whole = kb0 == 0 && kb1 == k_blocks;
-      // the position (and cache row) is read while the MMAs run
-      const C* cs = whole ? cache_row(cache, positions, max_position, m, valid, head < rot_heads)
-                          : nullptr;
+      // the row's position / cache row / norm factor are read while the MMAs run
+      RowState<C> rs;
+      if (whole) rs = row_state<C, EPI, NORM>(ep, m, valid, head);
       bool ready = tc::mbar_wait(&ctl->tmem_full[b], (uint32_t)(j >> 1) & 1u, kWaitLimitNs,
                                  &ctl->abort);
       ready = epi_all(ready);
@@ -490,7 +574,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                              (static_cast<uint32_t>(quarter * 32) << 16);
       if (whole) {
         T* o = out + (int64_t)(valid ? m : 0) * out_stride + (int64_t)head * HEAD;
-        finish_head_tmem<T, C, NEOX>(taddr, o, cs, valid && head < total_heads);
+        finish_head_tmem<T, C, EPI, NORM>(
+            taddr, o, rs,
+            EPI == EPI_RESIDUAL && ep.sumsq_out
+                ? ep.sumsq_out + (int64_t)(valid ? m : 0) * (ep.n_cols / SUMSQ_GROUP)
+                : nullptr,
+            head);
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ctl->tmem_empty[b]);
@@ -522,11 +611,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool last = *reinterpret_cast<volatile int*>(&ctl->last) != 0;
       epi_sync();  // ctl->last is rewritten by the next shared tile
       if (last)
-        fixup_tile<T, C, NEOX>(slots, sp, tile_u0, c0, c1,
-                               out + (int64_t)m0 * out_stride + (int64_t)nt * BN, out_stride,
-                               cache, positions, max_position, m0,
-                               min(BM, num_tokens - m0), nt * (BN / HEAD), rot_heads,
-                               total_heads, warp, lane);
+        fixup_tile<T, C, EPI, NORM>(slots, sp, tile_u0, c0, c1,
+                                    out + (int64_t)m0 * out_stride + (int64_t)nt * BN,
+                                    out_stride, ep, m0, min(BM, num_tokens - m0),
+                                    nt * (BN / HEAD), warp, lane);
     }
   }
 
@@ -558,22 +646,43 @@ QkvShape qkv_shape(int64_t num_tokens, int64_t hidden_size, int total_heads, int
   return s;
 }
 
+template <typename T, typename C, int EPI, bool NORM>
+int launch_gemm_epi(const CUtensorMap& ma, const CUtensorMap& mb, void* out, int64_t out_stride,
+                    int64_t num_tokens, const QkvShape& sh, const EpiParams& ep, void* workspace,
+                    int32_t* fault, int dev, cudaStream_t stream, const char* name) {
+  auto kernel = gemm_epi_kernel<T, C, EPI, NORM>;
+  cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), dev, SMEM_BYTES);
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  float* slots = static_cast<float*>(workspace);
+  int* counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + sh.slot_bytes);
+  err = launch(kernel, dim3((unsigned)sh.ctas), dim3(THREADS), SMEM_BYTES, stream, ma, mb,
+               static_cast<T*>(out), out_stride, (int)num_tokens, sh.m_tiles, sh.k_blocks, ep,
+               counters, slots, fault);
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  return PACE_OK;
+}
+
+EpiParams rope_params(const int64_t* positions, const void* cache, int64_t max_position,
+                      int rot_heads, int total_heads) {
+  EpiParams ep = {};
+  ep.positions = positions;
+  ep.cache = cache;
+  ep.max_position = max_position;
+  ep.rot_heads = rot_heads;
+  ep.total_heads = total_heads;
+  ep.n_cols = total_heads * HEAD;
+  return ep;
+}
+
 template <typename T, typename C, bool NEOX>
 int launch_qkv_rope(const CUtensorMap& ma, const CUtensorMap& mb, void* out, int64_t out_stride,
                     const int64_t* positions, const void* cache, int64_t max_position,
                     int64_t num_tokens, const QkvShape& sh, int rot_heads, int total_heads,
                     void* workspace, int32_t* fault, int dev, cudaStream_t stream) {
-  auto kernel = qkv_rope_kernel<T, C, NEOX>;
-  cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), dev, SMEM_BYTES);
-  if (err != cudaSuccess) return cuda_fail(err, "qkv_proj_rope (smem attribute)");
-  float* slots = static_cast<float*>(workspace);
-  int* counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + sh.slot_bytes);
-  err = launch(kernel, dim3((unsigned)sh.ctas), dim3(THREADS), SMEM_BYTES, stream, ma, mb,
-               static_cast<T*>(out), out_stride, positions, static_cast<const C*>(cache),
-               max_position, (int)num_tokens, sh.m_tiles, sh.k_blocks, rot_heads, total_heads,
-               counters, slots, fault);
-  if (err != cudaSuccess) return cuda_fail(err, "qkv_proj_rope");
-  return PACE_OK;
+  const EpiParams ep = rope_params(positions, cache, max_position, rot_heads, total_heads);
+  return launch_gemm_epi<T, C, NEOX ? EPI_ROPE_NEOX : EPI_ROPE_GPTJ, false>(
+      ma, mb, out, out_stride, num_tokens, sh, ep, workspace, fault, dev, stream,
+      "qkv_proj_rope");
 }
 
 }  // namespace
@@ -660,6 +769,153 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
   if (f32c) return neox ? PACE_QKV_ROPE(__half, float, true) : PACE_QKV_ROPE(__half, float, false);
   return neox ? PACE_QKV_ROPE(__half, __half, true) : PACE_QKV_ROPE(__half, __half, false);
 #undef PACE_QKV_ROPE
+}
+
+// ------------------------------------------------ RMSNorm around the GEMMs --
+namespace pace {
+namespace {
+// Shape and pointer checks shared by the two entry points below.
+int check_gemm_args(const char* name, int64_t num_tokens, int64_t n, int64_t k, int64_t a_stride,
+                    int64_t out_stride, int dtype, const void* out, const void* a, const void* w,
+                    const void* workspace) {
+  if (num_tokens < 0 || num_tokens > ((int64_t)1 << 24) || n <= 0 || k <= 0 ||
+      n > (int64_t)INT32_MAX || k > (int64_t)INT32_MAX * BK)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad shape", name);
+  if (dtype != PACE_BF16 && dtype != PACE_F16)
+    return fail(PACE_ERR_UNSUPPORTED_DTYPE, "%s: dtype %d must be bfloat16 or float16", name,
+                dtype);
+  if (a_stride < k || out_stride < n)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: row stride smaller than the row", name);
+  if (k % 8 != 0 || a_stride % 8 != 0 || out_stride % 8 != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: K and row strides must be multiples of 8 elements", name);
+  if (num_tokens == 0) return PACE_OK;
+  if (!out || !a || !w || !workspace) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(out) || !aligned16(a) || !aligned16(w) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: pointers must be 16-byte aligned (the workspace 256-byte aligned)", name);
+  return PACE_OK;
+}
+}  // namespace
+}  // namespace pace
+
+extern "C" size_t pace_linear_residual_workspace_size(int64_t num_tokens, int64_t n, int64_t k,
+                                                      int device) {
+  using namespace pace;
+  if (num_tokens <= 0 || n <= 0 || k <= 0 || n % HEAD != 0) return 0;
+  return qkv_shape(num_tokens, k, (int)(n / HEAD), sm_count(device)).workspace_bytes;
+}
+
+extern "C" int pace_linear_residual(void* residual, const void* input, const void* weight,
+                                    float* row_sumsq, int64_t num_tokens, int64_t n, int64_t k,
+                                    int64_t input_row_stride, int64_t residual_row_stride,
+                                    int dtype, void* workspace, size_t workspace_bytes,
+                                    int32_t* fault_flags, cudaStream_t stream) {
+  using namespace pace;
+  const char* name = "linear_residual";
+  int st = check_gemm_args(name, num_tokens, n, k, input_row_stride, residual_row_stride, dtype,
+                           residual, input, weight, workspace);
+  if (st != PACE_OK || num_tokens == 0) return st;
+  if (n % HEAD != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: n = %lld must be a multiple of %d", name,
+                (long long)n, HEAD);
+  StreamDeviceGuard guard(stream);
+  const int dev = guard.device();
+  const QkvShape sh = qkv_shape(num_tokens, k, (int)(n / HEAD), sm_count(dev));
+  if (workspace_bytes < sh.workspace_bytes)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
+                workspace_bytes, sh.workspace_bytes);
+  const bool bf16 = dtype == PACE_BF16;
+  CUtensorMap ma, mb;
+  st = tc::make_kmajor_map(&ma, input, bf16, num_tokens, k, input_row_stride, BM, name);
+  if (st != PACE_OK) return st;
+  st = tc::make_kmajor_map(&mb, weight, bf16, n, k, k, BN, name);
+  if (st != PACE_OK) return st;
+  EpiParams ep = {};
+  ep.sumsq_out = row_sumsq;
+  ep.n_cols = (int)n;
+  if (bf16)
+    return launch_gemm_epi<__nv_bfloat16, float, EPI_RESIDUAL, false>(
+        ma, mb, residual, residual_row_stride, num_tokens, sh, ep, workspace, fault_flags, dev,
+        stream, name);
+  return launch_gemm_epi<__half, float, EPI_RESIDUAL, false>(ma, mb, residual,
+                                                            residual_row_stride, num_tokens, sh,
+                                                            ep, workspace, fault_flags, dev,
+                                                            stream, name);
+}
+
+extern "C" int pace_qkv_proj_rmsnorm_rope(
+    void* qkv_out, const void* hidden, const void* folded_weight, const float* row_sumsq,
+    int64_t sumsq_groups, float epsilon, const int64_t* positions, int64_t num_tokens,
+    int64_t hidden_size, int num_heads, int num_kv_heads, int head_size,
+    int64_t hidden_row_stride, int64_t out_row_stride, const void* cos_sin_cache,
+    int cache_dtype, int rot_dim, int64_t max_position, int is_neox, int dtype, void* workspace,
+    size_t workspace_bytes, int32_t* fault_flags, cudaStream_t stream) {
+  using namespace pace;
+  const char* name = "qkv_proj_rmsnorm_rope";
+  if (num_heads < 0 || num_kv_heads < 0 || num_heads + num_kv_heads <= 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad head counts", name);
+  if (head_size != HEAD || rot_dim != head_size)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: head_size and rot_dim must both be %d (got %d, %d)", name, HEAD, head_size,
+                rot_dim);
+  if (cache_dtype != PACE_F32 && cache_dtype != dtype)
+    return fail(PACE_ERR_UNSUPPORTED_DTYPE,
+                "%s: cos_sin_cache dtype %d must be float32 or the q/k dtype %d", name,
+                cache_dtype, dtype);
+  if (sumsq_groups <= 0 || sumsq_groups > hidden_size)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: sumsq_groups %lld out of range", name,
+                (long long)sumsq_groups);
+  const int heads = num_heads + 2 * num_kv_heads;
+  const int64_t n = (int64_t)heads * head_size;
+  int st = check_gemm_args(name, num_tokens, n, hidden_size, hidden_row_stride, out_row_stride,
+                           dtype, qkv_out, hidden, folded_weight, workspace);
+  if (st != PACE_OK || num_tokens == 0) return st;
+  if (max_position <= 0) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: empty cos_sin_cache", name);
+  if (!positions || !cos_sin_cache || !row_sumsq)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(cos_sin_cache) || (reinterpret_cast<uintptr_t>(row_sumsq) & 15u) != 0 ||
+      sumsq_groups % 4 != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "%s: cache and row_sumsq must be 16-byte aligned, sumsq_groups a multiple of 4",
+                name);
+  StreamDeviceGuard guard(stream);
+  const int dev = guard.device();
+  const QkvShape sh = qkv_shape(num_tokens, hidden_size, heads, sm_count(dev));
+  if (workspace_bytes < sh.workspace_bytes)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
+                workspace_bytes, sh.workspace_bytes);
+  const bool bf16 = dtype == PACE_BF16;
+  CUtensorMap ma, mb;
+  st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
+  if (st != PACE_OK) return st;
+  st = tc::make_kmajor_map(&mb, folded_weight, bf16, n, hidden_size, hidden_size, BN, name);
+  if (st != PACE_OK) return st;
+  EpiParams ep = rope_params(positions, cos_sin_cache, max_position, num_heads + num_kv_heads,
+                             heads);
+  ep.sumsq_in = row_sumsq;
+  ep.sumsq_in_groups = (int)sumsq_groups;
+  ep.inv_k = 1.f / (float)hidden_size;
+  ep.eps = epsilon;
+#define PACE_QKV_NORM(T, C, E)                                                                  \
+  launch_gemm_epi<T, C, E, true>(ma, mb, qkv_out, out_row_stride, num_tokens, sh, ep, workspace, \
+                                 fault_flags, dev, stream, name)
+  const int epi = is_neox ? EPI_ROPE_NEOX : EPI_ROPE_GPTJ;
+  const bool f32c = cache_dtype == PACE_F32;
+  if (bf16) {
+    if (f32c)
+      return epi == EPI_ROPE_NEOX ? PACE_QKV_NORM(__nv_bfloat16, float, EPI_ROPE_NEOX)
+                                  : PACE_QKV_NORM(__nv_bfloat16, float, EPI_ROPE_GPTJ);
+    return epi == EPI_ROPE_NEOX ? PACE_QKV_NORM(__nv_bfloat16, __nv_bfloat16, EPI_ROPE_NEOX)
+                                : PACE_QKV_NORM(__nv_bfloat16, __nv_bfloat16, EPI_ROPE_GPTJ);
+  }
+  if (f32c)
+    return epi == EPI_ROPE_NEOX ? PACE_QKV_NORM(__half, float, EPI_ROPE_NEOX)
+                                : PACE_QKV_NORM(__half, float, EPI_ROPE_GPTJ);
+  return epi == EPI_ROPE_NEOX ? PACE_QKV_NORM(__half, __half, EPI_ROPE_NEOX)
+                              : PACE_QKV_NORM(__half, __half, EPI_ROPE_GPTJ);
+#undef PACE_QKV_NORM
 }
 
 // ------------------------------------------------- allocation-free variant --

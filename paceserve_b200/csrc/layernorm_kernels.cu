@@ -485,3 +485,62 @@ extern "C" int pace_fused_add_rms_norm(void* input, void* residual, const void* 
                                        residual_row_stride, stream, "fused_add_rms_norm");
   });
 }
+
+// Row sum-of-squares partials for the RMSNorm that the GEMM epilogues apply:
+// out[t, g] = sum of x[t, c]^2 over the 32 columns c of group g, in fp32.
+// One CTA per row, one thread per group (four 16-byte loads).
+namespace pace {
+namespace {
+template <typename T>
+__global__ void __launch_bounds__(256)
+    row_sumsq_kernel(float* __restrict__ out, const T* __restrict__ x, int groups,
+                     int64_t in_stride) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * in_stride;
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    float ss = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v[8];
+      Traits<T>::unpack(ld_nc_v4(xr + g * 32 + q * 8), v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+    }
+    out[row * groups + g] = ss;
+  }
+}
+}  // namespace
+}  // namespace pace
+
+extern "C" int pace_row_sumsq(float* row_sumsq, const void* input, int64_t num_tokens,
+                              int64_t hidden_size, int64_t input_row_stride, int dtype,
+                              cudaStream_t stream) {
+  using namespace pace;
+  if (num_tokens < 0 || num_tokens > INT32_MAX || hidden_size <= 0 || hidden_size % 32 != 0 ||
+      hidden_size / 32 > INT32_MAX)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "row_sumsq: hidden size %lld must be a positive multiple of 32",
+                (long long)hidden_size);
+  if (input_row_stride < hidden_size || input_row_stride % 8 != 0)
+    return fail(PACE_ERR_INVALID_ARGUMENT,
+                "row_sumsq: row stride must be >= the row and a multiple of 8");
+  if (num_tokens == 0) return PACE_OK;
+  if (!row_sumsq || !input) return fail(PACE_ERR_INVALID_ARGUMENT, "row_sumsq: null pointer");
+  if (!aligned16(input)) return fail(PACE_ERR_INVALID_ARGUMENT, "row_sumsq: input not 16-byte aligned");
+  StreamDeviceGuard guard(stream);
+  const int groups = (int)(hidden_size / 32);
+  const dim3 block((unsigned)(groups < 256 ? (groups + 31) / 32 * 32 : 256));
+  cudaError_t err;
+  if (dtype == PACE_BF16)
+    err = launch(row_sumsq_kernel<__nv_bfloat16>, dim3((unsigned)num_tokens), block, 0, stream,
+                 row_sumsq, static_cast<const __nv_bfloat16*>(input), groups, input_row_stride);
+  else if (dtype == PACE_F16)
+    err = launch(row_sumsq_kernel<__half>, dim3((unsigned)num_tokens), block, 0, stream,
+                 row_sumsq, static_cast<const __half*>(input), groups, input_row_stride);
+  else
+    return fail(PACE_ERR_UNSUPPORTED_DTYPE, "row_sumsq: dtype %d must be bfloat16 or float16", dtype);
+  if (err != cudaSuccess) return cuda_fail(err, "row_sumsq");
+  return PACE_OK;
+}

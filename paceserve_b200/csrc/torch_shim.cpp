@@ -258,6 +258,132 @@ void qkv_proj_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& weight, Tens
                op);
 }
 
+// Workspace for the tensor-core GEMMs (caller's, or the per-stream cache).
+Tensor gemm_workspace(const c10::optional<Tensor>& workspace, const at::Device& dev,
+                      cudaStream_t stream, size_t need, const char* op) {
+  if (workspace.has_value()) {
+    const Tensor& ws = *workspace;
+    TORCH_CHECK(ws.is_cuda() && ws.device() == dev && ws.is_contiguous() &&
+                    (size_t)ws.nbytes() >= need,
+                op, ": workspace must be a contiguous tensor of at least ", need, " bytes on ",
+                dev);
+    return ws;
+  }
+  return qkv_workspace(dev, stream, need);
+}
+
+// residual <- residual + input @ weight^T (o_proj / down_proj with the residual
+// add in the epilogue); row_sumsq (optional, float32 [T, n / 32]) receives the
+// new residual's sum-of-squares partials for the next RMSNorm.
+void linear_residual(Tensor& residual, Tensor& input, Tensor& weight,
+                     const c10::optional<Tensor>& row_sumsq,
+                     const c10::optional<Tensor>& workspace,
+                     const c10::optional<Tensor>& fault_flags) {
+  const char* op = "linear_residual";
+  check_cuda(input, op, "input");
+  check_same_device(residual, input, op);
+  check_same_device(weight, input, op);
+  TORCH_CHECK(input.scalar_type() == at::kBFloat16 || input.scalar_type() == at::kHalf, op,
+              ": input must be bfloat16 or float16");
+  TORCH_CHECK(residual.scalar_type() == input.scalar_type() &&
+                  weight.scalar_type() == input.scalar_type(),
+              op, ": residual, input and weight must share a dtype");
+  TORCH_CHECK(input.dim() == 2 && residual.dim() == 2 && weight.dim() == 2 &&
+                  weight.is_contiguous(),
+              op, ": input [T, k], residual [T, n] and a contiguous weight [n, k] expected");
+  const Rows a = rows_of(input, op, "input");
+  const Rows r = rows_of(residual, op, "residual");
+  TORCH_CHECK(r.rows == a.rows && weight.size(0) == r.width && weight.size(1) == a.width, op,
+              ": shapes do not match: input ", input.sizes(), ", residual ", residual.sizes(),
+              ", weight ", weight.sizes());
+  float* ss = nullptr;
+  if (row_sumsq.has_value()) {
+    const Tensor& t = *row_sumsq;
+    check_same_device(t, input, op);
+    TORCH_CHECK(t.scalar_type() == at::kFloat && t.is_contiguous() &&
+                    t.numel() >= a.rows * (r.width / 32),
+                op, ": row_sumsq must be a contiguous float32 tensor of T * n / 32 entries");
+    ss = t.data_ptr<float>();
+  }
+  const at::cuda::CUDAGuard guard(input.device());
+  if (a.rows == 0) return;
+  const cudaStream_t stream = stream_of(input);
+  const size_t need = pace_linear_residual_workspace_size(a.rows, r.width, a.width,
+                                                          input.device().index());
+  Tensor ws = gemm_workspace(workspace, input.device(), stream, need, op);
+  int32_t* fault = counter_ptr(fault_flags, input.device(), op, "fault_flags");
+  check_status(pace_linear_residual(residual.data_ptr(), input.data_ptr(), weight.data_ptr(), ss,
+                                    a.rows, r.width, a.width, a.stride, r.stride,
+                                    pace_dtype(input), ws.data_ptr(), (size_t)ws.nbytes(), fault,
+                                    stream),
+               op);
+}
+
+void row_sumsq(Tensor& out, Tensor& input) {
+  const char* op = "row_sumsq";
+  check_cuda(input, op, "input");
+  check_same_device(out, input, op);
+  const Rows a = rows_of(input, op, "input");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() &&
+                  out.numel() >= a.rows * (a.width / 32),
+              op, ": out must be a contiguous float32 tensor of T * hidden / 32 entries");
+  const at::cuda::CUDAGuard guard(input.device());
+  check_status(pace_row_sumsq(out.data_ptr<float>(), input.data_ptr(), a.rows, a.width,
+                              a.stride, pace_dtype(input), stream_of(input)),
+               op);
+}
+
+// qkv = rope(inv * (hidden @ folded_weight^T)), inv the rows' RMSNorm factor
+// from row_sumsq: input RMSNorm + qkv_proj + rotary_embedding in one GEMM.
+void qkv_proj_rmsnorm_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& folded_weight,
+                                       Tensor& row_sumsq, double epsilon, Tensor& positions,
+                                       int64_t head_size, int64_t num_heads,
+                                       int64_t num_kv_heads, Tensor& cos_sin_cache,
+                                       bool is_neox, const c10::optional<Tensor>& fault_flags,
+                                       const c10::optional<Tensor>& workspace) {
+  const char* op = "qkv_proj_rmsnorm_rotary_embedding";
+  check_cuda(hidden, op, "hidden");
+  for (const Tensor* t : {&qkv, &folded_weight, &row_sumsq, &positions, &cos_sin_cache})
+    check_same_device(*t, hidden, op);
+  TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 || hidden.scalar_type() == at::kHalf, op,
+              ": hidden must be bfloat16 or float16");
+  TORCH_CHECK(qkv.scalar_type() == hidden.scalar_type() &&
+                  folded_weight.scalar_type() == hidden.scalar_type(),
+              op, ": qkv, hidden and weight must share a dtype");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && positions.is_contiguous(), op,
+              ": positions must be a contiguous int64 tensor");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(), op,
+              ": cos_sin_cache must be a contiguous [max_position, rot_dim] tensor");
+  TORCH_CHECK(hidden.dim() == 2 && qkv.dim() == 2, op, ": hidden and qkv must be 2-D");
+  const Rows h = rows_of(hidden, op, "hidden");
+  const Rows o = rows_of(qkv, op, "qkv");
+  const int64_t n = (num_heads + 2 * num_kv_heads) * head_size;
+  TORCH_CHECK(o.rows == h.rows && o.width == n, op, ": qkv must be [T, ", n, "]");
+  TORCH_CHECK(folded_weight.dim() == 2 && folded_weight.is_contiguous() &&
+                  folded_weight.size(0) == n && folded_weight.size(1) == h.width,
+              op, ": weight must be a contiguous [", n, ", ", h.width, "] tensor");
+  TORCH_CHECK(row_sumsq.scalar_type() == at::kFloat && row_sumsq.is_contiguous() &&
+                  row_sumsq.numel() >= h.rows * (h.width / 32),
+              op, ": row_sumsq must be a contiguous float32 tensor of T * hidden / 32 entries");
+  TORCH_CHECK(positions.numel() >= h.rows, op, ": positions has too few entries");
+  const at::cuda::CUDAGuard guard(hidden.device());
+  if (h.rows == 0) return;
+  const cudaStream_t stream = stream_of(hidden);
+  const size_t need = pace_qkv_proj_rope_workspace_size(h.rows, h.width, (int)num_heads,
+                                                        (int)num_kv_heads, hidden.device().index());
+  Tensor ws = gemm_workspace(workspace, hidden.device(), stream, need, op);
+  int32_t* fault = counter_ptr(fault_flags, hidden.device(), op, "fault_flags");
+  check_status(pace_qkv_proj_rmsnorm_rope(
+                   qkv.data_ptr(), hidden.data_ptr(), folded_weight.data_ptr(),
+                   row_sumsq.data_ptr<float>(), h.width / 32, (float)epsilon,
+                   positions.data_ptr<int64_t>(), h.rows, h.width, (int)num_heads,
+                   (int)num_kv_heads, (int)head_size, h.stride, o.stride,
+                   cos_sin_cache.data_ptr(), pace_dtype(cos_sin_cache),
+                   (int)cos_sin_cache.size(1), cos_sin_cache.size(0), is_neox ? 1 : 0,
+                   pace_dtype(hidden), ws.data_ptr(), (size_t)ws.nbytes(), fault, stream),
+               op);
+}
+
 // ------------------------------------------------------------ activation --
 using ActFn = int (*)(void*, const void*, int64_t, int64_t, int64_t, int64_t, int, cudaStream_t);
 
@@ -787,6 +913,14 @@ PYBIND11_MODULE(_C, m) {
   auto ln = m.def_submodule("layernorm_ops");
   ln.def("rms_norm", &rms_norm, "Apply Root Mean Square (RMS) Normalization to the input tensor.",
          py::arg("out"), py::arg("input"), py::arg("weight"), py::arg("epsilon"));
+  ln.def("linear_residual", &linear_residual,
+         "residual += input @ weight^T on the tensor cores (o_proj / down_proj with the residual "
+         "add in the epilogue); row_sumsq receives the new rows' sum-of-squares partials.",
+         py::arg("residual"), py::arg("input"), py::arg("weight"),
+         py::arg("row_sumsq") = py::none(), py::arg("workspace") = py::none(),
+         py::arg("fault_flags") = py::none());
+  ln.def("row_sumsq", &row_sumsq, "out[t, g] = sum of input[t, 32g:32g+32]^2 (float32).",
+         py::arg("out"), py::arg("input"));
   ln.def("fused_add_rms_norm", &fused_add_rms_norm,
          "In place: residual += input; input = rms_norm(residual) * weight.", py::arg("input"),
          py::arg("residual"), py::arg("weight"), py::arg("epsilon"));
@@ -803,6 +937,14 @@ PYBIND11_MODULE(_C, m) {
          py::arg("head_size"), py::arg("num_heads"), py::arg("num_kv_heads"),
          py::arg("cos_sin_cache"), py::arg("is_neox"), py::arg("fault_flags") = py::none(),
          py::arg("workspace") = py::none());
+  pe.def("qkv_proj_rmsnorm_rotary_embedding", &qkv_proj_rmsnorm_rotary_embedding,
+         "qkv = rope(inv * (hidden @ folded_weight^T)): input RMSNorm (weight folded into the "
+         "projection, per-row factor from row_sumsq), qkv projection and rotary embedding in "
+         "one tensor-core GEMM.",
+         py::arg("qkv"), py::arg("hidden"), py::arg("folded_weight"), py::arg("row_sumsq"),
+         py::arg("epsilon"), py::arg("positions"), py::arg("head_size"), py::arg("num_heads"),
+         py::arg("num_kv_heads"), py::arg("cos_sin_cache"), py::arg("is_neox"),
+         py::arg("fault_flags") = py::none(), py::arg("workspace") = py::none());
   pe.def("qkv_proj_rope_workspace_size",
          [](int64_t num_tokens, int64_t hidden_size, int64_t num_heads, int64_t num_kv_heads,
             int64_t device) {

@@ -113,3 +113,16 @@ def test_new_gemm_ops_present_and_reject_cpu_tensors():
                                 torch.zeros(128, dtype=torch.int32),
                                 torch.zeros(1, dtype=torch.int32),
                                 torch.zeros(1, dtype=torch.int32), 4, None, 0)
+
+
+def test_fused_norm_gemm_ops_present():
+    assert _params(layernorm_ops.linear_residual)[:4] == ["residual", "input", "weight",
+                                                          "row_sumsq"]
+    assert _params(layernorm_ops.row_sumsq) == ["out", "input"]
+    assert _params(pos_encoding_ops.qkv_proj_rmsnorm_rotary_embedding)[:11] == [
+        "qkv", "hidden", "folded_weight", "row_sumsq", "epsilon", "positions", "head_size",
+        "num_heads", "num_kv_heads", "cos_sin_cache", "is_neox"]
+    w = torch.randn(6, 4).bfloat16()
+    nw = torch.tensor([1.0, 2.0, 0.5, -1.0]).bfloat16()
+    folded = paceserve_b200.fold_rmsnorm_weight(w, nw)
+    assert torch.equal(folded, (w.float() * nw.float()).bfloat16())
