@@ -1288,6 +1288,101 @@ def norm_gemm_bench(dev, tokens=(512, 2048), reps=10):
     return rows
 
 
+def layer_gemms_bench(dev, tokens=(512, 2048, 8192), reps=5):
+    """Everything in a Llama-3-8B decoder layer but attention, bf16: o_proj ->
+    residual add -> post-attention RMSNorm -> gate_up_proj -> SiLU-and-mul ->
+    down_proj -> residual add -> next input RMSNorm -> qkv_proj -> rope.
+    Fused: four tensor-core GEMMs (linear_residual, gate_up_silu with the norm
+    factor, linear_residual, qkv_proj_rmsnorm_rotary_embedding); the norms'
+    sums of squares come out of the residual GEMMs' epilogues.  Unfused: four
+    cuBLAS GEMMs with this package's fused_add_rms_norm (twice), silu_and_mul
+    and rotary_embedding between them.  Graphs over 2 weight sets (868 MB);
+    the final residual and qkv of the two paths compared within the bf16 rule.
+    Reported FLOP rate: the four GEMMs' 2 T (H H + 2 I H + I H + 6144 H)."""
+    import torch
+
+    import paceserve_b200 as pb
+
+    nbuf = 2
+    n = (NQ + 2 * NKV) * HD
+    g_ = torch.Generator(device=dev).manual_seed(23)
+
+    def w(rows, cols):
+        return (torch.randn(rows, cols, generator=g_, device=dev) / cols ** 0.5).bfloat16()
+
+    def nw():
+        return (torch.randn(H, generator=g_, device=dev) * 0.02 + 1).bfloat16()
+
+    sets = []
+    for _ in range(nbuf):
+        s_ = {"o": w(H, H), "gu": w(2 * I, H), "down": w(H, I), "qkv": w(n, H), "n2": nw(),
+              "n1": nw()}
+        s_["gu_f"] = pb.fold_rmsnorm_weight(s_["gu"], s_["n2"])
+        s_["qkv_f"] = pb.fold_rmsnorm_weight(s_["qkv"], s_["n1"])
+        sets.append(s_)
+    cache = rope_cache(dev)
+    flops_per_token = 2 * H * (H + 2 * I + I + n)
+    rows = []
+    for t in tokens:
+        attn = [torch.randn(t, H, generator=g_, device=dev).bfloat16() for _ in range(nbuf)]
+        res0 = [torch.randn(t, H, generator=g_, device=dev).bfloat16() for _ in range(nbuf)]
+        pos = torch.randint(0, MAX_POS, (t,), generator=g_, device=dev)
+        res_f = [r.clone() for r in res0]
+        res_u = [r.clone() for r in res0]
+        ss1 = [torch.empty(t, H // 32, device=dev) for _ in range(nbuf)]
+        ss2 = [torch.empty(t, H // 32, device=dev) for _ in range(nbuf)]
+        act = [torch.empty(t, I, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        gu = [torch.empty(t, 2 * I, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        xh = [torch.empty(t, H, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        qkv_f = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        qkv_u = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+
+        def fused():
+            for i, s_ in enumerate(sets):
+                pb.layernorm_ops.linear_residual(res_f[i], attn[i], s_["o"], ss1[i])
+                pb.activation_ops.gate_up_silu(act[i], res_f[i], s_["gu_f"], ss1[i], EPS)
+                pb.layernorm_ops.linear_residual(res_f[i], act[i], s_["down"], ss2[i])
+                pb.pos_encoding_ops.qkv_proj_rmsnorm_rotary_embedding(
+                    qkv_f[i], res_f[i], s_["qkv_f"], ss2[i], EPS, pos, HD, NQ, NKV, cache, True)
+
+        def unfused():
+            for i, s_ in enumerate(sets):
+                torch.matmul(attn[i], s_["o"].t(), out=xh[i])
+                pb.layernorm_ops.fused_add_rms_norm(xh[i], res_u[i], s_["n2"], EPS)
+                torch.matmul(xh[i], s_["gu"].t(), out=gu[i])
+                pb.activation_ops.silu_and_mul(act[i], gu[i])
+                torch.matmul(act[i], s_["down"].t(), out=xh[i])
+                pb.layernorm_ops.fused_add_rms_norm(xh[i], res_u[i], s_["n1"], EPS)
+                torch.matmul(xh[i], s_["qkv"].t(), out=qkv_u[i])
+                q = qkv_u[i]
+                pb.pos_encoding_ops.rotary_embedding(pos, q[:, : NQ * HD],
+                                                     q[:, NQ * HD: (NQ + NKV) * HD], HD, cache,
+                                                     True)
+
+        res = {"T": t}
+        for name, fn, resets in (("fused_us", fused, res_f), ("unfused_us", unfused, res_u)):
+            fn()  # eager once (workspace allocation outside capture)
+            gr = capture(fn)
+            res[name] = round(time_replays(gr, reps, 3) * 1e3 / (reps * nbuf), 3)
+            del gr
+            for r_, r0 in zip(resets, res0):  # the residual accumulated over replays
+                r_.copy_(r0)
+        fused()
+        unfused()
+        torch.cuda.synchronize()
+        res["fused_tflops"] = round(flops_per_token * t / res["fused_us"] / 1e6, 1)
+        res["unfused_tflops"] = round(flops_per_token * t / res["unfused_us"] / 1e6, 1)
+        res["speedup_vs_unfused"] = round(res["unfused_us"] / res["fused_us"], 3)
+        for key, a, b in (("rel_err_residual", res_f[0], res_u[0]),
+                          ("rel_err_qkv", qkv_f[0], qkv_u[0])):
+            a, b = a.float(), b.float()
+            res[key] = round(((a - b).abs().max() / b.abs().max()).item(), 5)
+        rows.append(res)
+        del attn, res0, res_f, res_u, ss1, ss2, act, gu, xh, qkv_f, qkv_u
+        torch.cuda.empty_cache()
+    return rows
+
+
 def _vllm_fused_experts():
     """vLLM's fused_experts (the library version of the reference's Triton
     fused MoE) as a baseline, or the reason it cannot run."""
@@ -1652,6 +1747,12 @@ def main():
                                      "the norm and rope in their epilogues, vs cuBLAS + this "
                                      "package's fused_add_rms_norm and rope",
                              "rows": norm_gemm_bench(dev)}
+        torch.cuda.empty_cache()
+        line["layer_gemms"] = {"what": "a Llama-3-8B layer minus attention (o_proj, residual, "
+                                       "RMSNorm, gate_up, SiLU-and-mul, down, residual, RMSNorm, "
+                                       "qkv, rope; bf16) as four tensor-core GEMMs with the rest "
+                                       "in their epilogues, vs cuBLAS + this package's ops",
+                               "peak_tflops": pk["bf16_tflops"], "rows": layer_gemms_bench(dev)}
         torch.cuda.empty_cache()
         line["moe_experts"] = {"what": "Mixtral-8x7B expert layer (E=8, top-2, 4096 -> 14336 -> "
                                        "4096, bf16): fused_experts on tcgen05 grouped GEMMs vs "

@@ -100,10 +100,14 @@ int pace_rotary_embedding(const int64_t* positions, void* query, void* key, int6
  * position lies outside [0, max_position) are stored unrotated.
  * workspace: device memory of at least pace_qkv_proj_rope_workspace_size()
  * bytes (for this shape and device), 256-byte aligned, ZERO-FILLED before its
- * first use; every call leaves it valid for the next (its tile counters back
- * at zero, at an offset that does not depend on the shape), so one zeroed
- * workspace serves any number of stream-ordered calls of any shapes that fit
- * in it.  Calls that may run concurrently need separate workspaces.
+ * first use; every call leaves it valid for the next (its grid-barrier count
+ * back at zero, at an offset that does not depend on the shape), so one
+ * zeroed workspace serves any number of stream-ordered calls of any shapes
+ * that fit in it.  Calls that may run concurrently need separate workspaces.
+ * The kernel's CTAs (at most one per SM) meet at one grid-wide barrier, so
+ * they must all be resident together: the call sizes its grid by the
+ * device's SM count, and a context limited to fewer SMs (an MPS share, a
+ * green context) sees the bounded wait expire instead.
  * fault_flags (optional device int32, may be NULL): bit 30 is OR-ed in when a
  * bounded device wait expires (the output is then incomplete and the
  * workspace must be zero-filled again before reuse).
@@ -159,6 +163,30 @@ int pace_qkv_proj_rmsnorm_rope(void* qkv_out, const void* hidden, const void* fo
                                const void* cos_sin_cache, int cache_dtype, int rot_dim,
                                int64_t max_position, int is_neox, int dtype, void* workspace,
                                size_t workspace_bytes, int32_t* fault_flags, cudaStream_t stream);
+
+/* pace_gate_up_silu: the MLP's gate_up_proj and SiLU-and-mul in one
+ * tensor-core GEMM (llama.py:70-104, activation_kernels.cu:15-45):
+ *   out[t, i] = silu(g) * u,  g = s[t] * (hidden[t] @ weight[i]^T),
+ *   u = s[t] * (hidden[t] @ weight[I + i]^T),
+ * weight = [gate rows; up rows] ([2 I, hidden_size], the layout of the
+ * reference's merged gate_up_proj, llama.py:452-469), out [T, I].  With
+ * row_sumsq null s = 1 (gate_up_proj on normalised rows); with row_sumsq the
+ * post-attention RMSNorm is a per-row factor s[t] = rsqrt(sum_g row_sumsq[t,
+ * g] / hidden_size + epsilon) and weight holds the norm weight folded in, as
+ * in pace_qkv_proj_rmsnorm_rope.  The [T, 2 I] gate_up activations are never
+ * written: gate and up stay in fp32 through the activation, where the
+ * reference rounds them to T first.  intermediate_size a multiple of 128;
+ * workspace as pace_qkv_proj_rope (zero-filled, left zeroed, size from
+ * pace_gate_up_silu_workspace_size).  Replaces gate_up_proj + silu_and_mul
+ * (llama.py:102-104).  No reference kernel. */
+size_t pace_gate_up_silu_workspace_size(int64_t num_tokens, int64_t hidden_size,
+                                        int64_t intermediate_size, int device);
+int pace_gate_up_silu(void* out, const void* hidden, const void* weight, const float* row_sumsq,
+                      int64_t sumsq_groups, float epsilon, int64_t num_tokens,
+                      int64_t hidden_size, int64_t intermediate_size,
+                      int64_t hidden_row_stride, int64_t out_row_stride, int dtype,
+                      void* workspace, size_t workspace_bytes, int32_t* fault_flags,
+                      cudaStream_t stream);
 
 /* Allocation-free variant of pace_qkv_proj_rope.  No counterpart in the
  * reference.  For callers that cannot allocate device memory: a plugin host

@@ -71,6 +71,12 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _P, _P, _P, c_int64, c_float, _P, c_int64, c_int64, c_int, c_int, c_int, c_int64,
          c_int64, _P, c_int, c_int, c_int64, c_int, c_int, _P, c_size_t, _P, _P],
     ),
+    "pace_gate_up_silu_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int]),
+    "pace_gate_up_silu": (
+        c_int,
+        [_P, _P, _P, _P, c_int64, c_float, c_int64, c_int64, c_int64, c_int64, c_int64, c_int,
+         _P, c_size_t, _P, _P],
+    ),
     "pace_moe_gather_rows": (
         c_int, [_P, _P, _P, c_int64, _P, c_int64, c_int, c_int64, c_int64, c_int64, c_int, _P]),
     "pace_moe_gemm": (

@@ -14,20 +14,24 @@
 // heads, so both halves of every NeoX pair (i, i + 64) and every GPT-J pair
 // (2i, 2i + 1) of a head sit in one tile), each tile into 64-element K blocks,
 // and the (tile, K block) units are split evenly over one persistent CTA per
-// SM.  A CTA whose range covers a whole tile finishes it directly; a tile
-// shared by several CTAs is finished by the CTA that contributes last: every
-// contributor stores its fp32 partial sum in the caller's workspace and counts
-// itself in the tile's counter, and the one that completes the count adds the
-// partials in segment order (so the result does not depend on which CTA came
-// last), rotates and stores.  No CTA ever waits for another.  At T=512 this
-// gives every SM 41.5 units instead of one or two whole tiles.
+// SM.  A CTA whose range covers a whole tile finishes it directly from TMEM.
+// Every other segment belongs to a tile shared by consecutive CTAs; its CTA
+// stores the fp32 partial sum in the caller's workspace.  When all CTAs have
+// stored theirs (one grid-wide barrier: the grid, at most one CTA per SM, is
+// co-resident, and the wait is bounded), every epilogue warp of the grid
+// takes a share of the shared tiles' (column pair, 32 rows) pieces, adds the
+// contributors' partials in CTA order (so the result does not depend on
+// timing), applies the epilogue and stores.  Spreading that reduction over
+// all SMs, instead of leaving each tile to one CTA, is what keeps decode-size
+// calls (T <= 128, six contributors per tile) short.  At T=512 this gives
+// every SM 41.5 units instead of one or two whole tiles.
 //
 // Inside a CTA: a 4-stage shared-memory ring of A (128 x 64) and B (256 x 64)
-// blocks filled by TMA (128-byte swizzle, no multicast; warp 4), tcgen05.mma
-// (M=128, N=256, K=16, fp32) issued by one thread of warp 5 into one of two
-// 256-column TMEM accumulators, and 4 epilogue warps (warp w owns TMEM lanes
-// 32w..32w+31, i.e. tile rows) that drain one accumulator while the MMAs fill
-// the other.  Every mbarrier wait is bounded by %globaltimer; on expiry the
+// blocks filled by TMA (128-byte swizzle, no multicast; warp 8), tcgen05.mma
+// (M=128, N=256, K=16, fp32) issued by one thread of warp 9 into one of two
+// 256-column TMEM accumulators, and 8 epilogue warps (warp w owns TMEM lanes
+// 32(w % 4)..+31, i.e. tile rows, and head w / 4 of the tile) that drain one
+// accumulator while the MMAs fill the other.  Every mbarrier wait is bounded by %globaltimer; on expiry the
 // CTA records bit 30 in the caller's fault word, stops issuing, waits (bounded
 // again) for its own copies and MMAs, frees TMEM and returns.
 #include <mutex>
@@ -59,9 +63,11 @@ struct Ctl {
   uint64_t drain;
   uint32_t tmem;
   int abort;
-  int last;  // epilogue: this CTA completes the current shared tile
+  int ready;  // epilogue: thread 0's wait for the tile's partials succeeded
 };
 static_assert(sizeof(Ctl) <= 256, "");
+// a finishing CTA stages the summed partials of one tile in the stage ring
+static_assert(SLOT_FLOATS * 4 <= STAGES * STAGE_BYTES, "");
 
 // Static split of the (tile, K block) units over the persistent CTAs.
 struct Split {
@@ -169,13 +175,15 @@ __device__ __forceinline__ float* slot_q(float* slot, int chunk, int q, int row)
 
 // ---- epilogue ------------------------------------------------------------
 // Epilogue kinds: the rotary embedding of the q/k heads (NeoX or GPT-J
-// pairs), or the residual add of o_proj / down_proj.  NORM (rope kinds):
+// pairs), the residual add of o_proj / down_proj, or SiLU-and-mul of the
+// gate/up projection (a tile holds 128 gate columns and the matching 128 up
+// columns; the output is 128 columns).  NORM (rope and gate/up kinds):
 // each row of the accumulator is first scaled by its RMSNorm factor
 // inv = rsqrt(sum of the row's squares / K + eps), from the sum-of-squares
 // partials the producer of the input rows wrote (the residual epilogue, or
 // pace_row_sumsq); the norm weight is folded into the GEMM weight by the
 // caller, so x_norm @ W^T = inv * (h @ (W diag(w))^T).
-constexpr int EPI_ROPE_NEOX = 0, EPI_ROPE_GPTJ = 1, EPI_RESIDUAL = 2;
+constexpr int EPI_ROPE_NEOX = 0, EPI_ROPE_GPTJ = 1, EPI_RESIDUAL = 2, EPI_GATEUP_SILU = 3;
 constexpr int SUMSQ_GROUP = 32;  // columns per sum-of-squares partial
 
 struct EpiParams {
@@ -257,8 +265,10 @@ __device__ __forceinline__ RowState<C> row_state(const EpiParams& ep, int m, boo
   RowState<C> s;
   s.cs = nullptr;
   s.inv = 1.f;
-  s.store = valid && (EPI == EPI_RESIDUAL ? head * HEAD < ep.n_cols : head < ep.total_heads);
-  if (EPI != EPI_RESIDUAL && valid && head < ep.rot_heads) {
+  s.store = valid && (EPI == EPI_GATEUP_SILU ? true
+                       : EPI == EPI_RESIDUAL  ? head * HEAD < ep.n_cols
+                                              : head < ep.total_heads);
+  if ((EPI == EPI_ROPE_NEOX || EPI == EPI_ROPE_GPTJ) && valid && head < ep.rot_heads) {
     const int64_t pos = ep.positions[m];
     if (pos >= 0 && pos < ep.max_position)
       s.cs = static_cast<const C*>(ep.cache) + pos * HEAD;
@@ -368,57 +378,174 @@ __device__ __forceinline__ void store_partial(uint32_t taddr, float* slot, int h
   }
 }
 
-// v[0..16) += the 16 floats of (chunk, row) in a partial slot.
-__device__ __forceinline__ void add16(float* v, const float* slot, int chunk, int row) {
+// SiLU-and-mul of 16 gate values a and 16 up values b (NORM: both scaled by the
+// row's factor first), into a.
+template <bool NORM>
+__device__ __forceinline__ void silu_mul16(float* a, const float* b, float inv) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float4 f = ld_cg_f4(slot_q(const_cast<float*>(slot), chunk, q, row));
-    v[4 * q] += f.x;
-    v[4 * q + 1] += f.y;
-    v[4 * q + 2] += f.z;
-    v[4 * q + 3] += f.w;
+  for (int e = 0; e < 16; ++e) {
+    const float g = NORM ? a[e] * inv : a[e];
+    const float u = NORM ? b[e] * inv : b[e];
+    a[e] = g / (1.f + __expf(-g)) * u;
   }
 }
 
-// Completion of a shared tile by the CTA that contributed last.  The 8
-// epilogue warps split it by column: warp w takes step w % 4 of head w / 4
-// for every valid row (lane + 32 p), so each load of a warp reads 32
-// consecutive rows of one chunk.  Partials are added in segment order.
+// A whole gate/up tile from TMEM: this thread's row, output columns
+// [64 half, 64 half + 64) = gate accumulator columns of the same offsets and
+// up columns 128 + those.  `taddr` addresses the row's accumulator start;
+// o is the row's output at the tile's first column.
+template <typename T, typename C, bool NORM>
+__device__ __forceinline__ void finish_gateup_tmem(uint32_t taddr, int half, T* o,
+                                                   const RowState<C>& s) {
+#pragma unroll 1
+  for (int i = 0; i < 4; ++i) {
+    const int c = half * 64 + 16 * i;
+    uint32_t rg[16], ru[16];
+    tc::tmem_ld16(taddr + c, rg);
+    tc::tmem_ld16(taddr + HEAD + c, ru);
+    tc::tmem_wait_ld(rg);
+    tc::tmem_wait_ld(ru);
+    float a[16], b[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      a[e] = __uint_as_float(rg[e]);
+      b[e] = __uint_as_float(ru[e]);
+    }
+    silu_mul16<NORM>(a, b, s.inv);
+    if (s.store) store16(o + c, a);
+  }
+}
+
+// Grid-wide barrier, called by thread 0 of every CTA once its epilogue
+// threads' partial stores are issued (and ordered before the call by the
+// epilogue barrier).  bar[0] counts arrivals and is reset to zero by the last
+// one, which then advances the generation bar[1] that the others wait on
+// (bounded).  The whole grid is co-resident (at most one CTA per SM, grid <=
+// SMs), so every CTA arrives.
+__device__ __forceinline__ bool grid_barrier(int* bar, int ctas, const Ctl* ctl) {
+  int gen0;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(gen0) : "l"(bar + 1) : "memory");
+  __threadfence();  // release the CTA's partials before its arrival
+  if (atomicAdd(bar, 1) == ctas - 1) {
+    atomicExch(bar, 0);  // re-armed for the next call
+    __threadfence();
+    atomicAdd(bar + 1, 1);
+    return true;
+  }
+  const uint64_t t0 = tc::globaltimer_ns();
+  for (;;) {
+    int g;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(g) : "l"(bar + 1) : "memory");
+    if (g != gen0) break;
+    if (*reinterpret_cast<const volatile int*>(&ctl->abort)) return false;
+    if (tc::globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    __nanosleep(64);
+  }
+  __threadfence();
+  return true;
+}
+
+// Partial slot of contributor c to shared tile t: a segment that starts at
+// the tile's first K block is its CTA's last (slot 2c + 1); any other is its
+// CTA's first (slot 2c).
+__device__ __forceinline__ const float* slot_of(const float* slots, int c, bool tile_start) {
+  return slots + (int64_t)(2 * c + (tile_start ? 1 : 0)) * SLOT_FLOATS;
+}
+
+// v_a, v_b += the partials of contributors c0..c1 at chunks ca, cb of tile row
+// r, in contributor order; two contributors' loads are issued together.
+__device__ __forceinline__ void sum_partials(float* va, float* vb, const float* slots, int c0,
+                                             int c1, int ca, int cb, int r) {
+#pragma unroll 1
+  for (int c = c0; c <= c1; c += 2) {
+    float4 x[2][8];
+    const bool two = c + 1 <= c1;
+    const float* s0 = slot_of(slots, c, c == c0);
+    const float* s1 = slot_of(slots, c + 1, false);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      x[0][q] = ld_cg_f4(slot_q(const_cast<float*>(s0), ca, q, r));
+      x[0][4 + q] = ld_cg_f4(slot_q(const_cast<float*>(s0), cb, q, r));
+      if (two) {
+        x[1][q] = ld_cg_f4(slot_q(const_cast<float*>(s1), ca, q, r));
+        x[1][4 + q] = ld_cg_f4(slot_q(const_cast<float*>(s1), cb, q, r));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !two) break;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        va[4 * q] += x[k][q].x;
+        va[4 * q + 1] += x[k][q].y;
+        va[4 * q + 2] += x[k][q].z;
+        va[4 * q + 3] += x[k][q].w;
+        vb[4 * q] += x[k][4 + q].x;
+        vb[4 * q + 1] += x[k][4 + q].y;
+        vb[4 * q + 2] += x[k][4 + q].z;
+        vb[4 * q + 3] += x[k][4 + q].w;
+      }
+    }
+  }
+}
+
+// Second phase: the shared stream-K tiles, finished by every epilogue warp of
+// the grid.  Work item = (tile, column pair p, 32-row group); a lane takes one
+// row, so each load of a warp reads 512 contiguous bytes of a slot.  Column
+// pair p: rope and residual, step p % 4 of head p / 4 (the two 16-column
+// pieces a step combines); gate/up, output columns [16p, 16p + 16) from gate
+// chunk p and up chunk 8 + p.
 template <typename T, typename C, int EPI, bool NORM>
-__device__ __forceinline__ void fixup_tile(const float* slots, const Split& sp, int64_t tile_u0,
-                                           int c0, int c1, T* out_tile, int64_t out_stride,
-                                           const EpiParams& ep, int m0, int valid_rows,
-                                           int head0, int warp, int lane) {
-  const int hh = warp / 4, i = warp % 4;
-  const int head = head0 + hh;
-  const int ca = hh * 8 + col_a<EPI>(i) / 16, cb = hh * 8 + col_b<EPI>(i) / 16;
+__device__ __forceinline__ void finish_shared_tiles(const float* slots, const Split& sp,
+                                                    int64_t t_stop, int64_t n_all, int n_tiles,
+                                                    T* out, int64_t out_stride,
+                                                    const EpiParams& ep, int num_tokens,
+                                                    int warp, int lane) {
+  const int64_t items = (n_all - t_stop) * 32;
   const int groups = ep.n_cols / SUMSQ_GROUP;
 #pragma unroll 1
-  for (int p = 0; p < BM / 32; ++p) {
-    const int r = lane + 32 * p;
-    if (r >= valid_rows) break;
-    const RowState<C> s = row_state<C, EPI, NORM>(ep, m0 + r, true, head);
-    if (!s.store) break;  // the head is past the output (odd head counts)
+  for (int64_t it = (int64_t)blockIdx.x * EPI_WARPS + warp; it < items;
+       it += (int64_t)gridDim.x * EPI_WARPS) {
+    const int64_t t = t_stop + it / 32;
+    const int p = (int)(it % 32) >> 2, g = (int)(it & 3);
+    const int64_t tile_u0 = (t - t_stop) * sp.k_blocks;
+    const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + sp.k_blocks - 1);
+    const int m0 = (int)(t / n_tiles) * BM, nt = (int)(t % n_tiles);
+    if (c0 == c1 || m0 + 32 * g >= num_tokens) continue;  // whole, or no rows here
+    const int r = 32 * g + lane, m = m0 + r;
+    if (m >= num_tokens) continue;
+    int ca, cb, head, i;
+    if (EPI == EPI_GATEUP_SILU) {
+      ca = p, cb = 8 + p, head = 0, i = 0;
+    } else {
+      const int hh = p >> 2;
+      i = p & 3;
+      ca = hh * 8 + col_a<EPI>(i) / 16;
+      cb = hh * 8 + col_b<EPI>(i) / 16;
+      head = nt * (BN / HEAD) + hh;
+    }
+    const RowState<C> s = row_state<C, EPI, NORM>(ep, m, true, head);
+    if (!s.store) continue;  // the head is past the output (odd head counts)
     float a[16], b[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
-#pragma unroll 2
-    for (int c = c0; c <= c1; ++c) {
-      const int slot = sp.start(c) >= tile_u0 ? 2 * c : 2 * c + 1;
-      const float* sl = slots + (int64_t)slot * SLOT_FLOATS;
-      add16(a, sl, ca, r);
-      add16(b, sl, cb, r);
+    sum_partials(a, b, slots, c0, c1, ca, cb, r);
+    if constexpr (EPI == EPI_GATEUP_SILU) {
+      silu_mul16<NORM>(a, b, s.inv);
+      store16(out + (int64_t)m * out_stride + (int64_t)nt * HEAD + 16 * p, a);
+    } else {
+      T* o = out + (int64_t)m * out_stride + (int64_t)head * HEAD;
+      const float ss = apply_step<T, C, EPI, NORM>(s, i, a, b, o);
+      if (EPI == EPI_RESIDUAL && ep.sumsq_out)
+        ep.sumsq_out[(int64_t)m * groups + head * 4 + i] = ss;
     }
-    T* o = out_tile + (int64_t)r * out_stride + hh * HEAD;
-    const float ss = apply_step<T, C, EPI, NORM>(s, i, a, b, o);
-    if (EPI == EPI_RESIDUAL && ep.sumsq_out)
-      ep.sumsq_out[(int64_t)(m0 + r) * groups + head * 4 + i] = ss;
   }
 }
 
 // One persistent CTA per SM (grid = min(SMs, units)); see the file comment.
-// slots: 2 partial tiles of BM x BN floats per CTA; counters: one int32 per
-// tile, zero before the call and left zero by it.
+// slots: 2 partial tiles of BM x BN floats per CTA; counters: the grid
+// barrier (arrival count, zero before the call and left zero by it;
+// generation).
 template <typename T, typename C, int EPI, bool NORM>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_epi_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -431,15 +558,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   Ctl* ctl = reinterpret_cast<Ctl*>(tiles + STAGES * STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
-  const int n_tiles = (ep.n_cols + BN - 1) / BN;
+  // output columns per tile: 128 for gate/up (each tile holds gate and up), else 256
+  const int n_tiles = EPI == EPI_GATEUP_SILU ? ep.n_cols / HEAD : (ep.n_cols + BN - 1) / BN;
   const int64_t n_all = (int64_t)m_tiles * n_tiles;
   const int64_t t_stop = n_all / gridDim.x * gridDim.x;  // first stream-K tile
   Split sp;  // stream-K split of the units of tiles [t_stop, n_all)
   sp.units = (n_all - t_stop) * k_blocks;
-  sp.ctas = gridDim.x;
+  // at most one CTA per unit, so every stream-K range is non-empty and a
+  // tile's contributors are consecutive CTAs
+  sp.ctas = (int)min((int64_t)gridDim.x, sp.units);
   sp.k_blocks = k_blocks;
-  const int64_t u_begin = sp.units > 0 ? sp.start(cta) : 0;
-  const int64_t u_end = sp.units > 0 ? sp.start(cta + 1) : 0;
+  const bool streams = cta < sp.ctas;
+  const int64_t u_begin = streams ? sp.start(cta) : 0;
+  const int64_t u_end = streams ? sp.start(cta + 1) : 0;
   const Walk walk0{cta, t_stop, (int64_t)gridDim.x, u_begin, u_end, k_blocks};
 
   pdl_launch_dependents();
@@ -478,7 +609,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       int64_t t;
       int kb0, kb1;
       while (ok && walk.next(t, kb0, kb1)) {
-        const int m0 = (int)(t / n_tiles) * BM, n0 = (int)(t % n_tiles) * BN;
+        const int m0 = (int)(t / n_tiles) * BM;
+        const int n0 = (int)(t % n_tiles) * (EPI == EPI_GATEUP_SILU ? HEAD : BN);
         for (int kb = kb0; kb < kb1; ++kb, ++i) {
           const int s = (int)(i % STAGES);
           const uint32_t use = (uint32_t)(i / STAGES);
@@ -490,7 +622,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint8_t* a = tiles + s * STAGE_BYTES;
           tc::mbar_arrive_expect_tx(&ctl->full[s], STAGE_BYTES);
           tc::tma_load_2d(a, &tm_a, kb * BK, m0, &ctl->full[s]);
-          tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
+          if (EPI == EPI_GATEUP_SILU) {
+            // gate rows [n0, n0 + 128) and up rows [n_cols + n0, +128)
+            tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
+            tc::tma_load_2d(a + A_BYTES + B_BYTES / 2, &tm_b, kb * BK, ep.n_cols + n0,
+                            &ctl->full[s]);
+          } else {
+            tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
+          }
         }
       }
       if (!ok) raise_fault(ctl, fault);
@@ -572,7 +711,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::tc_fence_after();
       const uint32_t taddr = tmem + (uint32_t)(b * BN + hh * HEAD) +
                              (static_cast<uint32_t>(quarter * 32) << 16);
-      if (whole) {
+      if (!whole) {
+        // a shared stream-K tile: publish this CTA's partial (finished in the
+        // second phase)
+        store_partial(taddr, const_cast<float*>(slot_of(slots, cta, kb0 == 0)), hh, row, valid);
+      } else if constexpr (EPI == EPI_GATEUP_SILU) {
+        T* o = out + (int64_t)(valid ? m : 0) * out_stride + (int64_t)nt * HEAD;
+        finish_gateup_tmem<T, C, NORM>(taddr - (uint32_t)(hh * HEAD), hh, o, rs);
+      } else {
         T* o = out + (int64_t)(valid ? m : 0) * out_stride + (int64_t)head * HEAD;
         finish_head_tmem<T, C, EPI, NORM>(
             taddr, o, rs,
@@ -580,41 +726,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ? ep.sumsq_out + (int64_t)(valid ? m : 0) * (ep.n_cols / SUMSQ_GROUP)
                 : nullptr,
             head);
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&ctl->tmem_empty[b]);
-        continue;
       }
-      // a shared tile: store this CTA's partial, then count it
-      const int64_t tile_u0 = (t - t_stop) * k_blocks;  // stream-K units are relative
-      const int my_slot = tile_u0 + kb0 == u_begin ? 2 * cta : 2 * cta + 1;
-      store_partial(taddr, slots + (int64_t)my_slot * SLOT_FLOATS, hh, row, valid);
-      // the accumulator is free for the segment after next
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&ctl->tmem_empty[b]);
-      // All epilogue threads' partial stores are ordered before thread 0's
-      // fence by the barrier; the fence (cumulative) then releases them at GPU
-      // scope before the count.  The CTA that completes the count fences
-      // again before its threads read the other partials.
+    }
+    if (sp.units > 0) {
+      // Second phase (same for every CTA: it depends on the shape only).  A
+      // CTA arrives even after a fault, so the others do not wait it out.
       epi_sync();
-      const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + k_blocks - 1);
-      if (threadIdx.x == 0) {
-        __threadfence();
-        const int prev = atomicAdd(&counters[t], 1);
-        const int last = prev == c1 - c0;
-        if (last) counters[t] = 0;  // ready for the next call
-        __threadfence();
-        ctl->last = last;
-      }
+      if (threadIdx.x == 0) ctl->ready = grid_barrier(counters, gridDim.x, ctl);
       epi_sync();
-      const bool last = *reinterpret_cast<volatile int*>(&ctl->last) != 0;
-      epi_sync();  // ctl->last is rewritten by the next shared tile
-      if (last)
-        fixup_tile<T, C, EPI, NORM>(slots, sp, tile_u0, c0, c1,
-                                    out + (int64_t)m0 * out_stride + (int64_t)nt * BN,
-                                    out_stride, ep, m0, min(BM, num_tokens - m0),
-                                    nt * (BN / HEAD), warp, lane);
+      if (*reinterpret_cast<volatile int*>(&ctl->ready) != 0)
+        finish_shared_tiles<T, C, EPI, NORM>(slots, sp, t_stop, n_all, n_tiles, out, out_stride,
+                                             ep, num_tokens, warp, lane);
+      else
+        raise_fault(ctl, fault);
     }
   }
 
@@ -916,6 +1043,78 @@ extern "C" int pace_qkv_proj_rmsnorm_rope(
   return epi == EPI_ROPE_NEOX ? PACE_QKV_NORM(__half, __half, EPI_ROPE_NEOX)
                               : PACE_QKV_NORM(__half, __half, EPI_ROPE_GPTJ);
 #undef PACE_QKV_NORM
+}
+
+// ------------------------------------------------------ gate/up + SiLU --
+// The MLP's first half in one GEMM: gate_up = x @ W^T with W = [gate rows;
+// up rows] ([2 I, H], the layout models/llama.py:70-104 builds and loads at
+// :452-469), then SiLU-and-mul (csrc/activation_kernels.cu:15-45) in the
+// epilogue, so the [T, 2 I] intermediate never reaches HBM.  With row_sumsq
+// the post-attention RMSNorm is applied as a per-row factor, W holding the
+// norm weight folded in (see pace_qkv_proj_rmsnorm_rope).
+extern "C" size_t pace_gate_up_silu_workspace_size(int64_t num_tokens, int64_t hidden_size,
+                                                   int64_t intermediate_size, int device) {
+  using namespace pace;
+  if (num_tokens <= 0 || hidden_size <= 0 || intermediate_size <= 0 ||
+      intermediate_size % HEAD != 0 || intermediate_size / HEAD > INT32_MAX / 2)
+    return 0;
+  // 2 I accumulator columns per row: one 256-column tile per 128 output columns
+  return qkv_shape(num_tokens, hidden_size, (int)(2 * intermediate_size / HEAD),
+                   sm_count(device))
+      .workspace_bytes;
+}
+
+extern "C" int pace_gate_up_silu(void* out, const void* hidden, const void* weight,
+                                 const float* row_sumsq, int64_t sumsq_groups, float epsilon,
+                                 int64_t num_tokens, int64_t hidden_size,
+                                 int64_t intermediate_size, int64_t hidden_row_stride,
+                                 int64_t out_row_stride, int dtype, void* workspace,
+                                 size_t workspace_bytes, int32_t* fault_flags,
+                                 cudaStream_t stream) {
+  using namespace pace;
+  const char* name = "gate_up_silu";
+  if (intermediate_size <= 0 || intermediate_size % HEAD != 0 ||
+      intermediate_size / HEAD > INT32_MAX / 2)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: intermediate size %lld must be a multiple of %d",
+                name, (long long)intermediate_size, HEAD);
+  int st = check_gemm_args(name, num_tokens, intermediate_size, hidden_size, hidden_row_stride,
+                           out_row_stride, dtype, out, hidden, weight, workspace);
+  if (st != PACE_OK || num_tokens == 0) return st;
+  if (row_sumsq) {
+    if (sumsq_groups <= 0 || sumsq_groups > hidden_size || sumsq_groups % 4 != 0 ||
+        (reinterpret_cast<uintptr_t>(row_sumsq) & 15u) != 0)
+      return fail(PACE_ERR_INVALID_ARGUMENT,
+                  "%s: row_sumsq must be 16-byte aligned with a multiple of 4 groups (<= %lld)",
+                  name, (long long)hidden_size);
+  }
+  StreamDeviceGuard guard(stream);
+  const int dev = guard.device();
+  const QkvShape sh =
+      qkv_shape(num_tokens, hidden_size, (int)(2 * intermediate_size / HEAD), sm_count(dev));
+  if (workspace_bytes < sh.workspace_bytes)
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
+                workspace_bytes, sh.workspace_bytes);
+  const bool bf16 = dtype == PACE_BF16;
+  CUtensorMap ma, mb;
+  st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM,
+                           name);
+  if (st != PACE_OK) return st;
+  // two 128-row boxes per stage: the gate rows and the up rows of the tile
+  st = tc::make_kmajor_map(&mb, weight, bf16, 2 * intermediate_size, hidden_size, hidden_size,
+                           HEAD, name);
+  if (st != PACE_OK) return st;
+  EpiParams ep = {};
+  ep.n_cols = (int)intermediate_size;
+  ep.sumsq_in = row_sumsq;
+  ep.sumsq_in_groups = (int)sumsq_groups;
+  ep.inv_k = 1.f / (float)hidden_size;
+  ep.eps = epsilon;
+#define PACE_GATE_UP(T, NORM)                                                                   \
+  launch_gemm_epi<T, float, EPI_GATEUP_SILU, NORM>(ma, mb, out, out_row_stride, num_tokens, sh, \
+                                                   ep, workspace, fault_flags, dev, stream, name)
+  if (bf16) return row_sumsq ? PACE_GATE_UP(__nv_bfloat16, true) : PACE_GATE_UP(__nv_bfloat16, false);
+  return row_sumsq ? PACE_GATE_UP(__half, true) : PACE_GATE_UP(__half, false);
+#undef PACE_GATE_UP
 }
 
 // ------------------------------------------------- allocation-free variant --

@@ -384,6 +384,54 @@ void qkv_proj_rmsnorm_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& fold
                op);
 }
 
+// out = silu(gate) * up with [gate | up] = hidden @ weight^T, weight =
+// [gate rows; up rows]: gate_up_proj + silu_and_mul in one GEMM.  With
+// row_sumsq the rows are RMS-normalised by a per-row factor (the norm weight
+// folded into `weight`).
+void gate_up_silu(Tensor& out, Tensor& hidden, Tensor& weight,
+                  const c10::optional<Tensor>& row_sumsq, double epsilon,
+                  const c10::optional<Tensor>& workspace,
+                  const c10::optional<Tensor>& fault_flags) {
+  const char* op = "gate_up_silu";
+  check_cuda(hidden, op, "hidden");
+  check_same_device(out, hidden, op);
+  check_same_device(weight, hidden, op);
+  TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 || hidden.scalar_type() == at::kHalf, op,
+              ": hidden must be bfloat16 or float16");
+  TORCH_CHECK(out.scalar_type() == hidden.scalar_type() &&
+                  weight.scalar_type() == hidden.scalar_type(),
+              op, ": out, hidden and weight must share a dtype");
+  TORCH_CHECK(hidden.dim() == 2 && out.dim() == 2 && weight.dim() == 2 && weight.is_contiguous(),
+              op, ": hidden [T, H], out [T, I] and a contiguous weight [2 I, H] expected");
+  const Rows h = rows_of(hidden, op, "hidden");
+  const Rows o = rows_of(out, op, "out");
+  TORCH_CHECK(o.rows == h.rows && weight.size(0) == 2 * o.width && weight.size(1) == h.width, op,
+              ": shapes do not match: hidden ", hidden.sizes(), ", out ", out.sizes(),
+              ", weight ", weight.sizes());
+  const float* ss = nullptr;
+  if (row_sumsq.has_value()) {
+    const Tensor& t = *row_sumsq;
+    check_same_device(t, hidden, op);
+    TORCH_CHECK(t.scalar_type() == at::kFloat && t.is_contiguous() &&
+                    t.numel() >= h.rows * (h.width / 32),
+                op, ": row_sumsq must be a contiguous float32 tensor of T * hidden / 32 entries");
+    ss = t.data_ptr<float>();
+  }
+  const at::cuda::CUDAGuard guard(hidden.device());
+  if (h.rows == 0) return;
+  const cudaStream_t stream = stream_of(hidden);
+  const size_t need = pace_gate_up_silu_workspace_size(h.rows, h.width, o.width,
+                                                       hidden.device().index());
+  TORCH_CHECK(need > 0, op, ": intermediate size ", o.width, " must be a multiple of 128");
+  Tensor ws = gemm_workspace(workspace, hidden.device(), stream, need, op);
+  int32_t* fault = counter_ptr(fault_flags, hidden.device(), op, "fault_flags");
+  check_status(pace_gate_up_silu(out.data_ptr(), hidden.data_ptr(), weight.data_ptr(), ss,
+                                 h.width / 32, (float)epsilon, h.rows, h.width, o.width, h.stride,
+                                 o.stride, pace_dtype(hidden), ws.data_ptr(), (size_t)ws.nbytes(),
+                                 fault, stream),
+               op);
+}
+
 // ------------------------------------------------------------ activation --
 using ActFn = int (*)(void*, const void*, int64_t, int64_t, int64_t, int64_t, int, cudaStream_t);
 
@@ -958,6 +1006,13 @@ PYBIND11_MODULE(_C, m) {
   auto act = m.def_submodule("activation_ops");
   act.def("silu_and_mul", &silu_and_mul, "Activation function used in SwiGLU.", py::arg("out"),
           py::arg("input"));
+  act.def("gate_up_silu", &gate_up_silu,
+          "out = silu(gate) * up, [gate | up] = hidden @ weight^T on the tensor cores "
+          "(gate_up_proj + silu_and_mul in one GEMM); with row_sumsq the post-attention "
+          "RMSNorm is a per-row factor and weight holds the norm weight folded in.",
+          py::arg("out"), py::arg("hidden"), py::arg("weight"),
+          py::arg("row_sumsq") = py::none(), py::arg("epsilon") = 1e-6,
+          py::arg("workspace") = py::none(), py::arg("fault_flags") = py::none());
   act.def("gelu_and_mul", &gelu_and_mul, "GeGLU: gelu(x[:, :d]) * x[:, d:] (erf GELU).",
           py::arg("out"), py::arg("input"));
   act.def("gelu_tanh_and_mul", &gelu_tanh_and_mul,

@@ -171,7 +171,7 @@ def test_c_abi_direct_call_and_workspace_reuse():
     ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     ref = reference(hidden, weight, positions, nq, nkv, hd, cache, True)
-    for _ in range(3):  # the workspace is left zeroed: reusable without clearing
+    for _ in range(3):  # the workspace is left valid: reusable without clearing
         out = torch.empty(T, n, dtype=torch.bfloat16, device=DEV)
         st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(),
                                     T, H, nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd,
@@ -179,8 +179,11 @@ def test_c_abi_direct_call_and_workspace_reuse():
         assert st == cabi.PACE_OK, lib.pace_last_error()
         torch.cuda.synchronize()
         check(out, ref, torch.bfloat16)
-    # the tile counters at the end of the workspace are back at zero
-    assert int(ws[-256:].sum().item()) == 0
+    # the grid barrier at the end of the workspace: arrival count re-armed,
+    # one generation per call, nothing else written
+    bar = ws[-256:].view(torch.int32)
+    assert bar[0].item() == 0 and bar[1].item() == 3
+    assert int(bar[2:].sum().item()) == 0
     st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(), T,
                                 H, nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd, 8192, 1,
                                 cabi.PACE_BF16, ws.data_ptr(), need - 1, None, stream)
@@ -235,6 +238,29 @@ def test_larger_and_odd_head_counts(T, H, nq, nkv):
                                                True)
     torch.cuda.synchronize()
     check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
+
+
+@pytest.mark.parametrize("extra", [1, 2, 9])
+def test_fewer_leftover_units_than_ctas(extra):
+    """SMs + extra tiles of 16 K blocks: after one data-parallel round the
+    leftover 16 * extra units are fewer than the CTAs, so the stream-K split
+    must use only as many CTAs as units (a tile's contributors consecutive).
+    Called twice: the tile counters must be left re-armed."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    T, H, hd, nkv = 128, 1024, 128, 2
+    nq = 2 * (sms + extra) - 2 * nkv  # (sms + extra) tiles of two heads
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, extra)
+    ref = reference(hidden, weight, positions, nq, nkv, hd, cache, True)
+    fault = torch.zeros(1, dtype=torch.int32, device=DEV)
+    args = (hidden.to(DEV), weight.to(DEV), positions.to(DEV), hd, nq, nkv, cache.to(DEV), True,
+            fault)
+    for _ in range(2):
+        qkv = torch.full((T, (nq + 2 * nkv) * hd), float("nan"), dtype=torch.bfloat16,
+                         device=DEV)
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv, *args)
+        torch.cuda.synchronize()
+        assert fault.item() == 0
+        check(qkv, ref, torch.bfloat16)
 
 
 def test_rejected_shapes():

@@ -126,3 +126,12 @@ def test_fused_norm_gemm_ops_present():
     nw = torch.tensor([1.0, 2.0, 0.5, -1.0]).bfloat16()
     folded = paceserve_b200.fold_rmsnorm_weight(w, nw)
     assert torch.equal(folded, (w.float() * nw.float()).bfloat16())
+
+
+def test_gate_up_silu_present_and_rejects_cpu_tensors():
+    assert _params(activation_ops.gate_up_silu)[:5] == ["out", "hidden", "weight", "row_sumsq",
+                                                       "epsilon"]
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        activation_ops.gate_up_silu(torch.empty(4, 128, dtype=torch.bfloat16),
+                                    torch.zeros(4, 64, dtype=torch.bfloat16),
+                                    torch.zeros(256, 64, dtype=torch.bfloat16))
