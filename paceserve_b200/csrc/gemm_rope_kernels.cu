@@ -42,32 +42,40 @@ namespace pace {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, HEAD = 128;
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+// Shared-memory stage ring by CTA mode.  One CTA per 128 x 256 tile: A
+// 128 x 64 and B 256 x 64 per stage, 4 stages of 48 KB.  A CTA pair per
+// 256 x 256 tile (tcgen05 cta_group::2: each CTA holds its 128 rows of A and
+// half of B, 128 x 64): 6 stages of 32 KB.  192 KB either way.
+template <bool PAIR>
+struct Ring {
+  static constexpr int kB = (PAIR ? BN / 2 : BN) * BK * 2;  // B bytes per CTA and stage
+  static constexpr int kStage = A_BYTES + kB;
+  static constexpr int kStages = PAIR ? 6 : 4;
+};
+constexpr int RING_BYTES = 4 * Ring<false>::kStage;
+static_assert(Ring<true>::kStages * Ring<true>::kStage == RING_BYTES, "");
+constexpr int MAX_STAGES = 6;
 constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter: one per head of the tile
 constexpr int THREADS = (EPI_WARPS + 2) * 32;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES = RING_BYTES + 1024 + 256;
 constexpr int SLOT_FLOATS = BM * BN;  // one partial tile
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
 constexpr int32_t kFaultTimeout = 1 << 30;
 constexpr int kEpiBarrier = 1;  // named barrier of the 256 epilogue threads
 
 struct Ctl {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[MAX_STAGES];
+  uint64_t empty[MAX_STAGES];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
   uint32_t tmem;
   int abort;
-  int ready;  // epilogue: thread 0's wait for the tile's partials succeeded
+  int ready;  // epilogue: thread 0's grid-barrier wait succeeded
 };
 static_assert(sizeof(Ctl) <= 256, "");
-// a finishing CTA stages the summed partials of one tile in the stage ring
-static_assert(SLOT_FLOATS * 4 <= STAGES * STAGE_BYTES, "");
 
 // Static split of the (tile, K block) units over the persistent CTAs.
 struct Split {
@@ -452,16 +460,17 @@ __device__ __forceinline__ const float* slot_of(const float* slots, int c, bool 
   return slots + (int64_t)(2 * c + (tile_start ? 1 : 0)) * SLOT_FLOATS;
 }
 
-// v_a, v_b += the partials of contributors c0..c1 at chunks ca, cb of tile row
-// r, in contributor order; two contributors' loads are issued together.
-__device__ __forceinline__ void sum_partials(float* va, float* vb, const float* slots, int c0,
-                                             int c1, int ca, int cb, int r) {
+// v_a, v_b += the partials of workers w0..w1 at chunks ca, cb of tile row r,
+// in worker order; worker w's CTA is w * mul + add (PAIR: the CTA of the pair
+// holding these rows).  Two workers' loads are issued together.
+__device__ __forceinline__ void sum_partials(float* va, float* vb, const float* slots, int w0,
+                                             int w1, int mul, int add, int ca, int cb, int r) {
 #pragma unroll 1
-  for (int c = c0; c <= c1; c += 2) {
+  for (int w = w0; w <= w1; w += 2) {
     float4 x[2][8];
-    const bool two = c + 1 <= c1;
-    const float* s0 = slot_of(slots, c, c == c0);
-    const float* s1 = slot_of(slots, c + 1, false);
+    const bool two = w + 1 <= w1;
+    const float* s0 = slot_of(slots, w * mul + add, w == w0);
+    const float* s1 = slot_of(slots, (w + 1) * mul + add, false);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       x[0][q] = ld_cg_f4(slot_q(const_cast<float*>(s0), ca, q, r));
@@ -495,22 +504,24 @@ __device__ __forceinline__ void sum_partials(float* va, float* vb, const float* 
 // pair p: rope and residual, step p % 4 of head p / 4 (the two 16-column
 // pieces a step combines); gate/up, output columns [16p, 16p + 16) from gate
 // chunk p and up chunk 8 + p.
-template <typename T, typename C, int EPI, bool NORM>
+template <typename T, typename C, int EPI, bool NORM, bool PAIR>
 __device__ __forceinline__ void finish_shared_tiles(const float* slots, const Split& sp,
                                                     int64_t t_stop, int64_t n_all, int n_tiles,
                                                     T* out, int64_t out_stride,
                                                     const EpiParams& ep, int num_tokens,
                                                     int warp, int lane) {
-  const int64_t items = (n_all - t_stop) * 32;
+  constexpr int HALVES = PAIR ? 2 : 1;  // 128-row halves of a tile
+  const int64_t items = (n_all - t_stop) * 32 * HALVES;
   const int groups = ep.n_cols / SUMSQ_GROUP;
 #pragma unroll 1
   for (int64_t it = (int64_t)blockIdx.x * EPI_WARPS + warp; it < items;
        it += (int64_t)gridDim.x * EPI_WARPS) {
-    const int64_t t = t_stop + it / 32;
+    const int64_t t = t_stop + it / (32 * HALVES);
+    const int h = PAIR ? (int)(it / 32) & 1 : 0;
     const int p = (int)(it % 32) >> 2, g = (int)(it & 3);
     const int64_t tile_u0 = (t - t_stop) * sp.k_blocks;
     const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + sp.k_blocks - 1);
-    const int m0 = (int)(t / n_tiles) * BM, nt = (int)(t % n_tiles);
+    const int m0 = (int)(t / n_tiles) * (HALVES * BM) + h * BM, nt = (int)(t % n_tiles);
     if (c0 == c1 || m0 + 32 * g >= num_tokens) continue;  // whole, or no rows here
     const int r = 32 * g + lane, m = m0 + r;
     if (m >= num_tokens) continue;
@@ -529,7 +540,7 @@ __device__ __forceinline__ void finish_shared_tiles(const float* slots, const Sp
     float a[16], b[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
-    sum_partials(a, b, slots, c0, c1, ca, cb, r);
+    sum_partials(a, b, slots, c0, c1, HALVES, h, ca, cb, r);
     if constexpr (EPI == EPI_GATEUP_SILU) {
       silu_mul16<NORM>(a, b, s.inv);
       store16(out + (int64_t)m * out_stride + (int64_t)nt * HEAD + 16 * p, a);
@@ -543,10 +554,14 @@ __device__ __forceinline__ void finish_shared_tiles(const float* slots, const Sp
 }
 
 // One persistent CTA per SM (grid = min(SMs, units)); see the file comment.
+// PAIR: clusters of two CTAs (launched with cluster dimension 2) share each
+// 256 x 256 tile through cta_group::2 MMAs; the pair is the unit of the
+// data-parallel and stream-K schedule ("worker"), each CTA keeps its 128 rows.
+// m_tiles counts tiles of 128 (one CTA) or 256 rows (PAIR).
 // slots: 2 partial tiles of BM x BN floats per CTA; counters: the grid
 // barrier (arrival count, zero before the call and left zero by it;
 // generation).
-template <typename T, typename C, int EPI, bool NORM>
+template <typename T, typename C, int EPI, bool NORM, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_epi_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     T* __restrict__ out, int64_t out_stride, int num_tokens, int m_tiles,
@@ -555,33 +570,39 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  Ctl* ctl = reinterpret_cast<Ctl*>(tiles + STAGES * STAGE_BYTES);
+  Ctl* ctl = reinterpret_cast<Ctl*>(tiles + RING_BYTES);
+  constexpr int NST = Ring<PAIR>::kStages, SB = Ring<PAIR>::kStage;
+  constexpr int PM = PAIR ? 2 * BM : BM;  // rows per tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
+  const uint32_t rank = PAIR ? tc::cluster_rank() : 0u;  // rows rank * 128 of the tile
+  const int worker = PAIR ? cta >> 1 : cta;
+  const int workers = PAIR ? (int)gridDim.x >> 1 : (int)gridDim.x;
   // output columns per tile: 128 for gate/up (each tile holds gate and up), else 256
   const int n_tiles = EPI == EPI_GATEUP_SILU ? ep.n_cols / HEAD : (ep.n_cols + BN - 1) / BN;
   const int64_t n_all = (int64_t)m_tiles * n_tiles;
-  const int64_t t_stop = n_all / gridDim.x * gridDim.x;  // first stream-K tile
+  const int64_t t_stop = n_all / workers * workers;  // first stream-K tile
   Split sp;  // stream-K split of the units of tiles [t_stop, n_all)
   sp.units = (n_all - t_stop) * k_blocks;
-  // at most one CTA per unit, so every stream-K range is non-empty and a
-  // tile's contributors are consecutive CTAs
-  sp.ctas = (int)min((int64_t)gridDim.x, sp.units);
+  // at most one worker per unit, so every stream-K range is non-empty and a
+  // tile's contributors are consecutive workers
+  sp.ctas = (int)min((int64_t)workers, sp.units);
   sp.k_blocks = k_blocks;
-  const bool streams = cta < sp.ctas;
-  const int64_t u_begin = streams ? sp.start(cta) : 0;
-  const int64_t u_end = streams ? sp.start(cta + 1) : 0;
-  const Walk walk0{cta, t_stop, (int64_t)gridDim.x, u_begin, u_end, k_blocks};
+  const bool streams = worker < sp.ctas;
+  const int64_t u_begin = streams ? sp.start(worker) : 0;
+  const int64_t u_end = streams ? sp.start(worker + 1) : 0;
+  const Walk walk0{worker, t_stop, (int64_t)workers, u_begin, u_end, k_blocks};
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       tc::mbar_init(&ctl->full[s], 1);
       tc::mbar_init(&ctl->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&ctl->tmem_full[b], 1);
-      tc::mbar_init(&ctl->tmem_empty[b], EPI_WARPS);
+      // PAIR: the epilogue warps of both CTAs free the leader's accumulator
+      tc::mbar_init(&ctl->tmem_empty[b], PAIR ? 2 * EPI_WARPS : EPI_WARPS);
     }
     tc::mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -591,9 +612,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc::tma_prefetch_desc(&tm_a);
     tc::tma_prefetch_desc(&tm_b);
   }
-  if (warp == 0) tc::tmem_alloc(&ctl->tmem, TMEM_COLS);
+  if (warp == 0) {
+    if constexpr (PAIR)
+      tc::tmem_alloc_pair(&ctl->tmem, TMEM_COLS);
+    else
+      tc::tmem_alloc(&ctl->tmem, TMEM_COLS);
+  }
   tc::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) tc::cluster_sync();  // both CTAs' barriers initialised
   tc::tc_fence_after();
   const uint32_t tmem = ctl->tmem;
   // hidden states, positions and the workspace may be in use by the previous
@@ -608,42 +635,55 @@ __global__ void __launch_bounds__(THREADS, 1)
       Walk walk = walk0;
       int64_t t;
       int kb0, kb1;
+      // PAIR: both CTAs' copies complete on the leader's barrier, which
+      // expects the bytes of both
+      const uint32_t full0 = PAIR ? tc::map_to_rank(&ctl->full[0], 0) : 0u;
       while (ok && walk.next(t, kb0, kb1)) {
-        const int m0 = (int)(t / n_tiles) * BM;
-        const int n0 = (int)(t % n_tiles) * (EPI == EPI_GATEUP_SILU ? HEAD : BN);
+        const int m0 = (int)(t / n_tiles) * PM + (int)rank * BM;
+        const int nt = (int)(t % n_tiles);
+        // B rows of this CTA: gate/up, gate rows [128 nt, +128) and up rows
+        // [n_cols + 128 nt, +128) (PAIR: rank 0 the gate, rank 1 the up rows);
+        // otherwise rows [256 nt, +256) (PAIR: rank r the 128 rows 128 r on)
+        const int n0 = EPI == EPI_GATEUP_SILU ? (int)rank * ep.n_cols + nt * HEAD
+                                              : nt * BN + (int)rank * (BN / 2);
         for (int kb = kb0; kb < kb1; ++kb, ++i) {
-          const int s = (int)(i % STAGES);
-          const uint32_t use = (uint32_t)(i / STAGES);
+          const int s = (int)(i % NST);
+          const uint32_t use = (uint32_t)(i / NST);
           if (use > 0 &&
               !tc::mbar_wait(&ctl->empty[s], (use - 1) & 1u, kWaitLimitNs, &ctl->abort)) {
             ok = false;
             break;
           }
-          uint8_t* a = tiles + s * STAGE_BYTES;
-          tc::mbar_arrive_expect_tx(&ctl->full[s], STAGE_BYTES);
-          tc::tma_load_2d(a, &tm_a, kb * BK, m0, &ctl->full[s]);
-          if (EPI == EPI_GATEUP_SILU) {
-            // gate rows [n0, n0 + 128) and up rows [n_cols + n0, +128)
-            tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
-            tc::tma_load_2d(a + A_BYTES + B_BYTES / 2, &tm_b, kb * BK, ep.n_cols + n0,
-                            &ctl->full[s]);
+          uint8_t* a = tiles + s * SB;
+          if constexpr (PAIR) {
+            const uint32_t bar = full0 + (uint32_t)(s * sizeof(uint64_t));
+            if (rank == 0) tc::mbar_arrive_expect_tx(&ctl->full[s], 2 * SB);
+            tc::tma_load_2d_pair(a, &tm_a, kb * BK, m0, bar);
+            tc::tma_load_2d_pair(a + A_BYTES, &tm_b, kb * BK, n0, bar);
           } else {
+            tc::mbar_arrive_expect_tx(&ctl->full[s], SB);
+            tc::tma_load_2d(a, &tm_a, kb * BK, m0, &ctl->full[s]);
             tc::tma_load_2d(a + A_BYTES, &tm_b, kb * BK, n0, &ctl->full[s]);
+            if (EPI == EPI_GATEUP_SILU)
+              tc::tma_load_2d(a + A_BYTES + HEAD * BK * 2, &tm_b, kb * BK, ep.n_cols + n0,
+                              &ctl->full[s]);
           }
         }
       }
       if (!ok) raise_fault(ctl, fault);
       // every copy issued has landed before the CTA's shared memory is released
-      // (immediate when the MMAs consumed them all)
-      for (int64_t q = i > STAGES ? i - STAGES : 0; q < i; ++q)
-        tc::mbar_wait(&ctl->full[q % STAGES], (uint32_t)(q / STAGES) & 1u, kWaitLimitNs,
-                      nullptr);
+      // (immediate when the MMAs consumed them all).  PAIR: the leader's
+      // barriers count both CTAs' copies; the partner leaves only after the
+      // leader, at the closing cluster barrier.
+      if (!PAIR || rank == 0)
+        for (int64_t q = i > NST ? i - NST : 0; q < i; ++q)
+          tc::mbar_wait(&ctl->full[q % NST], (uint32_t)(q / NST) & 1u, kWaitLimitNs, nullptr);
     }
   } else if (warp == EPI_WARPS + 1) {
     // ---- MMA issuer ----------------------------------------------------
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-      constexpr uint32_t idesc = tc::umma_idesc_f16(kBf16, BM, BN);
+      constexpr uint32_t idesc = tc::umma_idesc_f16(kBf16, PM, BN);
       int64_t i = 0;
       int j = 0;
       bool ok = true;
@@ -661,32 +701,50 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * BN);
         for (int kb = kb0; kb < kb1; ++kb, ++i) {
-          const int s = (int)(i % STAGES);
-          if (!tc::mbar_wait(&ctl->full[s], (uint32_t)(i / STAGES) & 1u, kWaitLimitNs,
+          const int s = (int)(i % NST);
+          if (!tc::mbar_wait(&ctl->full[s], (uint32_t)(i / NST) & 1u, kWaitLimitNs,
                              &ctl->abort)) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const uint32_t a_addr = tc::smem_u32(tiles + s * STAGE_BYTES);
+          const uint32_t a_addr = tc::smem_u32(tiles + s * SB);
           const uint64_t ad = tc::umma_desc_sw128(a_addr);
           const uint64_t bd = tc::umma_desc_sw128(a_addr + A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            tc::umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-          tc::umma_commit(&ctl->empty[s]);
+          for (int k = 0; k < BK / 16; ++k) {
+            if constexpr (PAIR)
+              tc::umma_f16_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else
+              tc::umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          // the stage is free in both CTAs (PAIR) once these MMAs complete
+          if constexpr (PAIR)
+            tc::umma_commit_pair_both(&ctl->empty[s]);
+          else
+            tc::umma_commit(&ctl->empty[s]);
         }
-        if (ok) tc::umma_commit(&ctl->tmem_full[b]);
+        if (ok) {
+          if constexpr (PAIR)
+            tc::umma_commit_pair_both(&ctl->tmem_full[b]);
+          else
+            tc::umma_commit(&ctl->tmem_full[b]);
+        }
       }
       if (!ok) raise_fault(ctl, fault);
       // every MMA issued has completed before TMEM is freed
-      tc::umma_commit(&ctl->drain);
+      if constexpr (PAIR)
+        tc::umma_commit_pair(&ctl->drain);
+      else
+        tc::umma_commit(&ctl->drain);
       tc::mbar_wait(&ctl->drain, 0, kWaitLimitNs, nullptr);
     }
   } else {
     // ---- epilogue: warp w drains TMEM lanes 32 (w % 4) .. +31, head w / 4 ----
     const int quarter = warp % 4, hh = warp / 4;
     const int row = quarter * 32 + lane;
+    // the accumulator buffers are freed on the pair leader's barriers
+    const uint32_t tmem_empty0 = PAIR ? tc::map_to_rank(&ctl->tmem_empty[0], 0) : 0u;
     int j = 0;
     Walk walk = walk0;
     int64_t t;
@@ -694,7 +752,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (; walk.next(t, kb0, kb1); ++j) {
       const int b = j & 1;
       const int mt = (int)(t / n_tiles), nt = (int)(t % n_tiles);
-      const int m0 = mt * BM, m = m0 + row;
+      const int m0 = mt * PM + (int)rank * BM, m = m0 + row;
       const bool valid = m < num_tokens;
       const int head = nt * (BN / HEAD) + hh;
       const bool whole = kb0 == 0 && kb1 == k_blocks;
@@ -729,7 +787,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&ctl->tmem_empty[b]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          tc::mbar_arrive_cluster(tmem_empty0 + (uint32_t)(b * sizeof(uint64_t)));
+        else
+          tc::mbar_arrive(&ctl->tmem_empty[b]);
+      }
     }
     if (sp.units > 0) {
       // Second phase (same for every CTA: it depends on the shape only).  A
@@ -738,8 +801,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (threadIdx.x == 0) ctl->ready = grid_barrier(counters, gridDim.x, ctl);
       epi_sync();
       if (*reinterpret_cast<volatile int*>(&ctl->ready) != 0)
-        finish_shared_tiles<T, C, EPI, NORM>(slots, sp, t_stop, n_all, n_tiles, out, out_stride,
-                                             ep, num_tokens, warp, lane);
+        finish_shared_tiles<T, C, EPI, NORM, PAIR>(slots, sp, t_stop, n_all, n_tiles, out,
+                                                   out_stride, ep, num_tokens, warp, lane);
       else
         raise_fault(ctl, fault);
     }
@@ -747,46 +810,111 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
+  if constexpr (PAIR) {
+    // neither CTA leaves (nor frees TMEM) while its partner may still signal
+    // its barriers or read its shared memory
+    tc::cluster_sync();
+    if (warp == 0) tc::tmem_dealloc_pair(tmem, TMEM_COLS);
+  } else {
+    if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
 }
 
 // ---------------------------------------------------------------- host ----
 // Workspace layout: 2 partial slots per SM (a fixed size for the device),
-// then one int32 counter per tile.  The counters sit at the same offset for
-// every shape, so a workspace that a call of one shape left zeroed is valid
-// for a call of any other shape that fits in it.
+// then the grid barrier, in an area of one int32 per 128-row tile.  The
+// barrier sits at the same offset for every shape, so a workspace that a call
+// of one shape left valid serves a call of any other shape that fits in it.
 struct QkvShape {
   int m_tiles, n_tiles, k_blocks, ctas;
+  bool pair;  // 256-row tiles on CTA pairs (m_tiles counts those)
   size_t slot_bytes, workspace_bytes;
 };
 
+// CTA pairs once the rows fill more than one 128-row tile: they halve the B
+// bytes each SM stages per MMA.  One 128-row tile runs on single CTAs (a
+// pair would spend half its MMAs on rows that do not exist).
 QkvShape qkv_shape(int64_t num_tokens, int64_t hidden_size, int total_heads, int sms) {
   QkvShape s;
-  s.m_tiles = (int)ceil_div(num_tokens, BM);
+  s.pair = num_tokens > BM;
+  s.m_tiles = (int)ceil_div(num_tokens, s.pair ? 2 * BM : BM);
   s.n_tiles = (int)ceil_div((int64_t)total_heads * HEAD, BN);
   s.k_blocks = (int)ceil_div(hidden_size, BK);
   const int64_t units = (int64_t)s.m_tiles * s.n_tiles * s.k_blocks;
-  s.ctas = (int)(units < sms ? units : sms);
+  const int64_t workers = s.pair ? sms / 2 : sms;
+  s.ctas = (int)((units < workers ? units : workers) * (s.pair ? 2 : 1));
   s.slot_bytes = (size_t)2 * sms * SLOT_FLOATS * sizeof(float);
   s.workspace_bytes =
-      s.slot_bytes + ((size_t)s.m_tiles * s.n_tiles * sizeof(int) + 255) / 256 * 256;
+      s.slot_bytes +
+      ((size_t)ceil_div(num_tokens, BM) * s.n_tiles * sizeof(int) + 255) / 256 * 256;
   return s;
+}
+
+// Clusters of two of this kernel that the device holds at once, per device
+// (the same for every instantiation: one CTA per SM by shared memory).
+template <typename K>
+int pairs_resident(K kernel, int dev) {
+  static std::mutex mu;
+  static int cached[64] = {};
+  if (dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) return 0;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <typename T, typename C, int EPI, bool NORM, bool PAIR>
+int launch_gemm_epi_mode(const CUtensorMap& ma, const CUtensorMap& mb, void* out,
+                         int64_t out_stride, int64_t num_tokens, const QkvShape& sh,
+                         const EpiParams& ep, void* workspace, int32_t* fault, int dev,
+                         cudaStream_t stream, const char* name) {
+  auto kernel = gemm_epi_kernel<T, C, EPI, NORM, PAIR>;
+  cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), dev, SMEM_BYTES);
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  float* slots = static_cast<float*>(workspace);
+  int* counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + sh.slot_bytes);
+  int ctas = sh.ctas;
+  if constexpr (PAIR) {
+    // every CTA must be resident at once (grid barrier)
+    const int pairs = pairs_resident(kernel, dev);
+    if (pairs < 1)
+      return fail(PACE_ERR_CUDA, "%s: the device holds no cluster of two CTAs", name);
+    ctas = ctas < 2 * pairs ? ctas : 2 * pairs;
+    err = launch_pairs(kernel, dim3((unsigned)ctas), dim3(THREADS), SMEM_BYTES, stream, ma, mb,
+                       static_cast<T*>(out), out_stride, (int)num_tokens, sh.m_tiles,
+                       sh.k_blocks, ep, counters, slots, fault);
+  } else {
+    err = launch(kernel, dim3((unsigned)ctas), dim3(THREADS), SMEM_BYTES, stream, ma, mb,
+                 static_cast<T*>(out), out_stride, (int)num_tokens, sh.m_tiles, sh.k_blocks, ep,
+                 counters, slots, fault);
+  }
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  return PACE_OK;
 }
 
 template <typename T, typename C, int EPI, bool NORM>
 int launch_gemm_epi(const CUtensorMap& ma, const CUtensorMap& mb, void* out, int64_t out_stride,
                     int64_t num_tokens, const QkvShape& sh, const EpiParams& ep, void* workspace,
                     int32_t* fault, int dev, cudaStream_t stream, const char* name) {
-  auto kernel = gemm_epi_kernel<T, C, EPI, NORM>;
-  cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), dev, SMEM_BYTES);
-  if (err != cudaSuccess) return cuda_fail(err, name);
-  float* slots = static_cast<float*>(workspace);
-  int* counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + sh.slot_bytes);
-  err = launch(kernel, dim3((unsigned)sh.ctas), dim3(THREADS), SMEM_BYTES, stream, ma, mb,
-               static_cast<T*>(out), out_stride, (int)num_tokens, sh.m_tiles, sh.k_blocks, ep,
-               counters, slots, fault);
-  if (err != cudaSuccess) return cuda_fail(err, name);
-  return PACE_OK;
+  if (sh.pair)
+    return launch_gemm_epi_mode<T, C, EPI, NORM, true>(ma, mb, out, out_stride, num_tokens, sh,
+                                                       ep, workspace, fault, dev, stream, name);
+  return launch_gemm_epi_mode<T, C, EPI, NORM, false>(ma, mb, out, out_stride, num_tokens, sh,
+                                                      ep, workspace, fault, dev, stream, name);
 }
 
 EpiParams rope_params(const int64_t* positions, const void* cache, int64_t max_position,
@@ -877,7 +1005,8 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
   CUtensorMap ma, mb;
   int st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
   if (st != PACE_OK) return st;
-  st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
+  st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size,
+                           sh.pair ? BN / 2 : BN, name);
   if (st != PACE_OK) return st;
   const int rot_heads = num_heads + num_kv_heads;
 #define PACE_QKV_ROPE(T, C, NX)                                                                 \
@@ -957,7 +1086,7 @@ extern "C" int pace_linear_residual(void* residual, const void* input, const voi
   CUtensorMap ma, mb;
   st = tc::make_kmajor_map(&ma, input, bf16, num_tokens, k, input_row_stride, BM, name);
   if (st != PACE_OK) return st;
-  st = tc::make_kmajor_map(&mb, weight, bf16, n, k, k, BN, name);
+  st = tc::make_kmajor_map(&mb, weight, bf16, n, k, k, sh.pair ? BN / 2 : BN, name);
   if (st != PACE_OK) return st;
   EpiParams ep = {};
   ep.sumsq_out = row_sumsq;
@@ -1017,7 +1146,8 @@ extern "C" int pace_qkv_proj_rmsnorm_rope(
   CUtensorMap ma, mb;
   st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
   if (st != PACE_OK) return st;
-  st = tc::make_kmajor_map(&mb, folded_weight, bf16, n, hidden_size, hidden_size, BN, name);
+  st = tc::make_kmajor_map(&mb, folded_weight, bf16, n, hidden_size, hidden_size,
+                           sh.pair ? BN / 2 : BN, name);
   if (st != PACE_OK) return st;
   EpiParams ep = rope_params(positions, cos_sin_cache, max_position, num_heads + num_kv_heads,
                              heads);
@@ -1213,7 +1343,9 @@ extern "C" int pace_qkv_proj_rope_no_alloc(
   void* scratch = no_alloc_scratch(dev);
   if (!scratch) return PACE_ERR_CUDA;
   QkvShape sh = qkv_shape(num_tokens, hidden_size, heads, sm_count(dev));
-  if (sh.ctas > kNoAllocCtas) sh.ctas = kNoAllocCtas;
+  // at most kNoAllocCtas CTAs have slots (an even number on CTA pairs)
+  const int cap = sh.pair ? kNoAllocCtas / 2 * 2 : kNoAllocCtas;
+  if (sh.ctas > cap) sh.ctas = cap;
   sh.slot_bytes = kNoAllocSlotBytes;
   // The counters must start at zero.  Calls leave them zero, but one whose
   // wait expired may not: clear them on the stream first (no allocation).
@@ -1224,7 +1356,8 @@ extern "C" int pace_qkv_proj_rope_no_alloc(
   CUtensorMap ma, mb;
   int st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
   if (st != PACE_OK) return st;
-  st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size, BN, name);
+  st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size,
+                           sh.pair ? BN / 2 : BN, name);
   if (st != PACE_OK) return st;
   const int rot_heads = num_heads + num_kv_heads;
 #define PACE_QKV_ROPE_NA(T, C, NX)                                                               \
