@@ -180,9 +180,10 @@ def test_c_abi_direct_call_and_workspace_reuse():
         torch.cuda.synchronize()
         check(out, ref, torch.bfloat16)
     # the grid barrier at the end of the workspace: arrival count re-armed,
-    # one generation per call, nothing else written
+    # one generation per call that needed it (none when the tiles run
+    # data-parallel), nothing else written
     bar = ws[-256:].view(torch.int32)
-    assert bar[0].item() == 0 and bar[1].item() == 3
+    assert bar[0].item() == 0 and bar[1].item() in (0, 3)
     assert int(bar[2:].sum().item()) == 0
     st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(), T,
                                 H, nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd, 8192, 1,
