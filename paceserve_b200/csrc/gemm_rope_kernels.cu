@@ -301,9 +301,26 @@ __device__ __forceinline__ RowState<C> row_state(const EpiParams& ep, int m, boo
 // Step i of a row: a (at col_a) and b (at col_b) hold the fp32 accumulator;
 // o is the row's output at the head's first column.  Returns the step's sum
 // of squares (residual), else 0.
+// The memory inputs of step i besides the accumulator: rope, the cache's 16
+// cos and 16 sin values (x, y) when the head is rotated; residual, the 16 + 16
+// residual values at col_a / col_b.  Issued early by callers that can overlap
+// them with other loads.
+template <typename T, typename C, int EPI>
+__device__ __forceinline__ void load_step_inputs(const RowState<C>& s, int i, const T* o,
+                                                 float* x, float* y) {
+  if (EPI == EPI_RESIDUAL) {
+    if (s.store) {
+      load16(o + col_a<EPI>(i), x);
+      load16(o + col_b<EPI>(i), y);
+    }
+  } else if (s.cs) {
+    load_step_cs(s.cs, i, x, y);
+  }
+}
+
 template <typename T, typename C, int EPI, bool NORM>
-__device__ __forceinline__ float apply_step(const RowState<C>& s, int i, float* a, float* b,
-                                            T* o) {
+__device__ __forceinline__ float apply_step_with(const RowState<C>& s, int i, float* a, float* b,
+                                                 T* o, const float* x, const float* y) {
   if (NORM) {
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
@@ -314,26 +331,29 @@ __device__ __forceinline__ float apply_step(const RowState<C>& s, int i, float* 
   float ss = 0.f;
   if (EPI == EPI_RESIDUAL) {
     if (s.store) {
-      float ra[16], rb[16];
-      load16(o + col_a<EPI>(i), ra);
-      load16(o + col_b<EPI>(i), rb);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        a[e] = Traits<T>::round(a[e] + ra[e]);
-        b[e] = Traits<T>::round(b[e] + rb[e]);
+        a[e] = Traits<T>::round(a[e] + x[e]);
+        b[e] = Traits<T>::round(b[e] + y[e]);
         ss += a[e] * a[e] + b[e] * b[e];
       }
     }
   } else if (s.cs) {
-    float cv[16], sv[16];
-    load_step_cs(s.cs, i, cv, sv);
-    rotate<EPI>(a, b, cv, sv);
+    rotate<EPI>(a, b, x, y);
   }
   if (s.store) {
     store16(o + col_a<EPI>(i), a);
     store16(o + col_b<EPI>(i), b);
   }
   return ss;
+}
+
+template <typename T, typename C, int EPI, bool NORM>
+__device__ __forceinline__ float apply_step(const RowState<C>& s, int i, float* a, float* b,
+                                            T* o) {
+  float x[16], y[16];
+  load_step_inputs<T, C, EPI>(s, i, o, x, y);
+  return apply_step_with<T, C, EPI, NORM>(s, i, a, b, o, x, y);
 }
 
 // A whole tile from TMEM: this thread's row, one head (128 columns at TMEM
@@ -427,29 +447,31 @@ __device__ __forceinline__ void finish_gateup_tmem(uint32_t taddr, int half, T* 
 // Grid-wide barrier, called by thread 0 of every CTA once its epilogue
 // threads' partial stores are issued (and ordered before the call by the
 // epilogue barrier).  bar[0] counts arrivals and is reset to zero by the last
-// one, which then advances the generation bar[1] that the others wait on
-// (bounded).  The whole grid is co-resident (at most one CTA per SM, grid <=
-// SMs), so every CTA arrives.
+// one, which then advances the generation bar[kGenOffset] (its own 128-byte
+// line, so the waiters' polls do not contend with the arrivals) that the
+// others wait on (bounded).  The whole grid is co-resident (at most one CTA
+// per SM, grid <= SMs or resident CTA pairs), so every CTA arrives.
+constexpr int kGenOffset = 32;
 __device__ __forceinline__ bool grid_barrier(int* bar, int ctas, const Ctl* ctl) {
+  int* gen = bar + kGenOffset;
   int gen0;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(gen0) : "l"(bar + 1) : "memory");
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(gen0) : "l"(gen) : "memory");
   __threadfence();  // release the CTA's partials before its arrival
   if (atomicAdd(bar, 1) == ctas - 1) {
-    atomicExch(bar, 0);  // re-armed for the next call
-    __threadfence();
-    atomicAdd(bar + 1, 1);
+    *reinterpret_cast<volatile int*>(bar) = 0;  // re-armed for the next call
+    __threadfence();  // acquire the other CTAs' arrivals (and their partials)
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(gen), "r"(gen0 + 1) : "memory");
     return true;
   }
   const uint64_t t0 = tc::globaltimer_ns();
   for (;;) {
     int g;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(g) : "l"(bar + 1) : "memory");
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(g) : "l"(gen) : "memory");
     if (g != gen0) break;
     if (*reinterpret_cast<const volatile int*>(&ctl->abort)) return false;
     if (tc::globaltimer_ns() - t0 > kWaitLimitNs) return false;
-    __nanosleep(64);
+    __nanosleep(20);
   }
-  __threadfence();
   return true;
 }
 
@@ -462,27 +484,26 @@ __device__ __forceinline__ const float* slot_of(const float* slots, int c, bool 
 
 // v_a, v_b += the partials of workers w0..w1 at chunks ca, cb of tile row r,
 // in worker order; worker w's CTA is w * mul + add (PAIR: the CTA of the pair
-// holding these rows).  Two workers' loads are issued together.
+// holding these rows).  The loads of two workers are issued together.
 __device__ __forceinline__ void sum_partials(float* va, float* vb, const float* slots, int w0,
                                              int w1, int mul, int add, int ca, int cb, int r) {
+  constexpr int NB = 2;
 #pragma unroll 1
-  for (int w = w0; w <= w1; w += 2) {
-    float4 x[2][8];
-    const bool two = w + 1 <= w1;
-    const float* s0 = slot_of(slots, w * mul + add, w == w0);
-    const float* s1 = slot_of(slots, (w + 1) * mul + add, false);
+  for (int w = w0; w <= w1; w += NB) {
+    float4 x[NB][8];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      x[0][q] = ld_cg_f4(slot_q(const_cast<float*>(s0), ca, q, r));
-      x[0][4 + q] = ld_cg_f4(slot_q(const_cast<float*>(s0), cb, q, r));
-      if (two) {
-        x[1][q] = ld_cg_f4(slot_q(const_cast<float*>(s1), ca, q, r));
-        x[1][4 + q] = ld_cg_f4(slot_q(const_cast<float*>(s1), cb, q, r));
+    for (int k = 0; k < NB; ++k) {
+      if (w + k > w1) break;
+      float* sl = const_cast<float*>(slot_of(slots, (w + k) * mul + add, w + k == w0));
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        x[k][q] = ld_cg_f4(slot_q(sl, ca, q, r));
+        x[k][4 + q] = ld_cg_f4(slot_q(sl, cb, q, r));
       }
     }
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      if (k == 1 && !two) break;
+    for (int k = 0; k < NB; ++k) {
+      if (w + k > w1) break;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         va[4 * q] += x[k][q].x;
@@ -535,18 +556,24 @@ __device__ __forceinline__ void finish_shared_tiles(const float* slots, const Sp
       cb = hh * 8 + col_b<EPI>(i) / 16;
       head = nt * (BN / HEAD) + hh;
     }
+    // The row's own inputs (position, norm partials, then the cache row or
+    // residual values) are requested before and between the partial loads,
+    // so their latencies overlap; a head past the output (odd head counts)
+    // only skips the store.
     const RowState<C> s = row_state<C, EPI, NORM>(ep, m, true, head);
-    if (!s.store) continue;  // the head is past the output (odd head counts)
+    T* o = out + (int64_t)m * out_stride + (int64_t)head * HEAD;
+    float x[16], y[16];
+    if constexpr (EPI != EPI_GATEUP_SILU) load_step_inputs<T, C, EPI>(s, i, o, x, y);
     float a[16], b[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
     sum_partials(a, b, slots, c0, c1, HALVES, h, ca, cb, r);
+    if (!s.store) continue;
     if constexpr (EPI == EPI_GATEUP_SILU) {
       silu_mul16<NORM>(a, b, s.inv);
       store16(out + (int64_t)m * out_stride + (int64_t)nt * HEAD + 16 * p, a);
     } else {
-      T* o = out + (int64_t)m * out_stride + (int64_t)head * HEAD;
-      const float ss = apply_step<T, C, EPI, NORM>(s, i, a, b, o);
+      const float ss = apply_step_with<T, C, EPI, NORM>(s, i, a, b, o, x, y);
       if (EPI == EPI_RESIDUAL && ep.sumsq_out)
         ep.sumsq_out[(int64_t)m * groups + head * 4 + i] = ss;
     }
