@@ -256,6 +256,10 @@ __device__ __forceinline__ void load16(const T* p, float* v) {
   Traits<T>::unpack(ld_v4(p + 8), v + 8);
 }
 
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // What one thread needs to finish its head of one tile row.
 template <typename C>
 struct RowState {
@@ -278,8 +282,14 @@ __device__ __forceinline__ RowState<C> row_state(const EpiParams& ep, int m, boo
                                               : head < ep.total_heads);
   if ((EPI == EPI_ROPE_NEOX || EPI == EPI_ROPE_GPTJ) && valid && head < ep.rot_heads) {
     const int64_t pos = ep.positions[m];
-    if (pos >= 0 && pos < ep.max_position)
+    if (pos >= 0 && pos < ep.max_position) {
       s.cs = static_cast<const C*>(ep.cache) + pos * HEAD;
+      // the epilogue's four steps read the whole cache row (read-only data,
+      // cached in L1): fetch it while the MMAs run
+#pragma unroll
+      for (int l = 0; l < HEAD * (int)sizeof(C); l += 128)
+        prefetch_l1(reinterpret_cast<const char*>(s.cs) + l);
+    }
   }
   if (NORM && valid) {
     const float* p = ep.sumsq_in + (int64_t)m * ep.sumsq_in_groups;
@@ -362,11 +372,18 @@ __device__ __forceinline__ float apply_step(const RowState<C>& s, int i, float* 
 template <typename T, typename C, int EPI, bool NORM>
 __device__ __forceinline__ void finish_head_tmem(uint32_t taddr, T* o, const RowState<C>& s,
                                                  float* ss_out, int head) {
-#pragma unroll 1
+  if (EPI == EPI_RESIDUAL && s.store) {
+    // the head's residual values: 128 columns, fetched while TMEM is read
+#pragma unroll
+    for (int l = 0; l < HEAD * (int)sizeof(T); l += 128)
+      prefetch_l1(reinterpret_cast<const char*>(o) + l);
+  }
+  // step i + 1's TMEM loads are issued before step i is processed
+  uint32_t ra[16], rb[16];
+  tc::tmem_ld16(taddr + col_a<EPI>(0), ra);
+  tc::tmem_ld16(taddr + col_b<EPI>(0), rb);
+#pragma unroll
   for (int i = 0; i < 4; ++i) {
-    uint32_t ra[16], rb[16];
-    tc::tmem_ld16(taddr + col_a<EPI>(i), ra);
-    tc::tmem_ld16(taddr + col_b<EPI>(i), rb);
     tc::tmem_wait_ld(ra);
     tc::tmem_wait_ld(rb);
     float a[16], b[16];
@@ -374,6 +391,10 @@ __device__ __forceinline__ void finish_head_tmem(uint32_t taddr, T* o, const Row
     for (int e = 0; e < 16; ++e) {
       a[e] = __uint_as_float(ra[e]);
       b[e] = __uint_as_float(rb[e]);
+    }
+    if (i < 3) {
+      tc::tmem_ld16(taddr + col_a<EPI>(i + 1), ra);
+      tc::tmem_ld16(taddr + col_b<EPI>(i + 1), rb);
     }
     const float ss = apply_step<T, C, EPI, NORM>(s, i, a, b, o);
     if (EPI == EPI_RESIDUAL && ss_out && s.store) ss_out[head * 4 + i] = ss;
