@@ -150,6 +150,13 @@ __device__ __forceinline__ void st_v4(void* p, const uint4& v) {
                "r"(v.w)
                : "memory");
 }
+// 32 bytes in one store (sm_100 256-bit access): a whole L2 sector per thread.
+// p must be 32-byte aligned.
+__device__ __forceinline__ void st_v8(void* p, const uint4& lo, const uint4& hi) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(lo.x),
+               "r"(lo.y), "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
 
 // ------------------------------------------------------------ dtype traits --
 template <typename T>

@@ -74,10 +74,18 @@ __device__ __forceinline__ bool epi_all(bool pred) {
   return r != 0;
 }
 
+// 16 values of a tile row: one 32-byte store when the address allows (a full
+// sector; the rows of a warp are far apart, so two 16-byte stores would each
+// write half sectors), else two 16-byte stores.
 template <typename T>
 __device__ __forceinline__ void store16(T* p, const float* v) {
-  st_v4(p, Traits<T>::pack(v));
-  st_v4(p + 8, Traits<T>::pack(v + 8));
+  const uint4 lo = Traits<T>::pack(v), hi = Traits<T>::pack(v + 8);
+  if ((reinterpret_cast<uintptr_t>(p) & 31u) == 0) {
+    st_v8(p, lo, hi);
+  } else {
+    st_v4(p, lo);
+    st_v4(p + 8, hi);
+  }
 }
 
 // silu(x) = x / (1 + e^-x) in fp32 (csrc/activation_kernels.cu:8-12).
