@@ -74,6 +74,8 @@ struct Ctl {
   uint32_t tmem;
   int abort;
   int ready;  // epilogue: thread 0's grid-barrier wait succeeded
+  int nfin;   // decode sizes: shared tiles this CTA completed last ...
+  int fin[4];  // ... (at most 2: a range's first and last segment)
 };
 static_assert(sizeof(Ctl) <= 256, "");
 
@@ -481,6 +483,8 @@ __device__ __forceinline__ void finish_gateup_tmem(uint32_t taddr, int half, T* 
 // others wait on (bounded).  The whole grid is co-resident (at most one CTA
 // per SM, grid <= SMs or resident CTA pairs), so every CTA arrives.
 constexpr int kGenOffset = 32;
+// Per-tile arrival counters (decode sizes) start after the barrier's 256 bytes.
+constexpr int kTileCounterOffset = 64;
 __device__ __forceinline__ bool grid_barrier(int* bar, int ctas, const Ctl* ctl) {
   int* gen = bar + kGenOffset;
   int gen0;
@@ -548,64 +552,49 @@ __device__ __forceinline__ void sum_partials(float* va, float* vb, const float* 
   }
 }
 
-// Second phase: the shared stream-K tiles, finished by every epilogue warp of
-// the grid.  Work item = (tile, column pair p, 32-row group); a lane takes one
-// row, so each load of a warp reads 512 contiguous bytes of a slot.  Column
-// pair p: rope and residual, step p % 4 of head p / 4 (the two 16-column
-// pieces a step combines); gate/up, output columns [16p, 16p + 16) from gate
-// chunk p and up chunk 8 + p.
+// One piece of a shared stream-K tile: column pair p, 32-row group g of the
+// tile's 128-row half h, summed over the contributing workers w0..w1 and
+// finished.  A lane takes one row, so each load of a warp reads 512
+// contiguous bytes of a slot.  Column pair p: rope and residual, step p % 4
+// of head p / 4 (the two 16-column pieces a step combines); gate/up, output
+// columns [16p, 16p + 16) from gate chunk p and up chunk 8 + p.
 template <typename T, typename C, int EPI, bool NORM, bool PAIR>
-__device__ __forceinline__ void finish_shared_tiles(const float* slots, const Split& sp,
-                                                    int64_t t_stop, int64_t n_all, int n_tiles,
-                                                    T* out, int64_t out_stride,
-                                                    const EpiParams& ep, int num_tokens,
-                                                    int warp, int lane) {
-  constexpr int HALVES = PAIR ? 2 : 1;  // 128-row halves of a tile
-  const int64_t items = (n_all - t_stop) * 32 * HALVES;
-  const int groups = ep.n_cols / SUMSQ_GROUP;
-#pragma unroll 1
-  for (int64_t it = (int64_t)blockIdx.x * EPI_WARPS + warp; it < items;
-       it += (int64_t)gridDim.x * EPI_WARPS) {
-    const int64_t t = t_stop + it / (32 * HALVES);
-    const int h = PAIR ? (int)(it / 32) & 1 : 0;
-    const int p = (int)(it % 32) >> 2, g = (int)(it & 3);
-    const int64_t tile_u0 = (t - t_stop) * sp.k_blocks;
-    const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + sp.k_blocks - 1);
-    const int m0 = (int)(t / n_tiles) * (HALVES * BM) + h * BM, nt = (int)(t % n_tiles);
-    if (c0 == c1 || m0 + 32 * g >= num_tokens) continue;  // whole, or no rows here
-    const int r = 32 * g + lane, m = m0 + r;
-    if (m >= num_tokens) continue;
-    int ca, cb, head, i;
-    if (EPI == EPI_GATEUP_SILU) {
-      ca = p, cb = 8 + p, head = 0, i = 0;
-    } else {
-      const int hh = p >> 2;
-      i = p & 3;
-      ca = hh * 8 + col_a<EPI>(i) / 16;
-      cb = hh * 8 + col_b<EPI>(i) / 16;
-      head = nt * (BN / HEAD) + hh;
-    }
-    // The row's own inputs (position, norm partials, then the cache row or
-    // residual values) are requested before and between the partial loads,
-    // so their latencies overlap; a head past the output (odd head counts)
-    // only skips the store.
-    const RowState<C> s = row_state<C, EPI, NORM>(ep, m, true, head);
-    T* o = out + (int64_t)m * out_stride + (int64_t)head * HEAD;
-    float x[16], y[16];
-    if constexpr (EPI != EPI_GATEUP_SILU) load_step_inputs<T, C, EPI>(s, i, o, x, y);
-    float a[16], b[16];
+__device__ __forceinline__ void finish_piece(const float* slots, int w0, int w1, int m0, int nt,
+                                             int p, int g, int h, T* out, int64_t out_stride,
+                                             const EpiParams& ep, int num_tokens, int lane) {
+  constexpr int HALVES = PAIR ? 2 : 1;
+  const int r = 32 * g + lane, m = m0 + r;
+  if (m >= num_tokens) return;
+  int ca, cb, head, i;
+  if (EPI == EPI_GATEUP_SILU) {
+    ca = p, cb = 8 + p, head = 0, i = 0;
+  } else {
+    const int hh = p >> 2;
+    i = p & 3;
+    ca = hh * 8 + col_a<EPI>(i) / 16;
+    cb = hh * 8 + col_b<EPI>(i) / 16;
+    head = nt * (BN / HEAD) + hh;
+  }
+  // The row's own inputs (position, norm partials, then the cache row or
+  // residual values) are requested before and between the partial loads,
+  // so their latencies overlap; a head past the output (odd head counts)
+  // only skips the store.
+  const RowState<C> s = row_state<C, EPI, NORM>(ep, m, true, head);
+  T* o = out + (int64_t)m * out_stride + (int64_t)head * HEAD;
+  float x[16], y[16];
+  if constexpr (EPI != EPI_GATEUP_SILU) load_step_inputs<T, C, EPI>(s, i, o, x, y);
+  float a[16], b[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
-    sum_partials(a, b, slots, c0, c1, HALVES, h, ca, cb, r);
-    if (!s.store) continue;
-    if constexpr (EPI == EPI_GATEUP_SILU) {
-      silu_mul16<NORM>(a, b, s.inv);
-      store16(out + (int64_t)m * out_stride + (int64_t)nt * HEAD + 16 * p, a);
-    } else {
-      const float ss = apply_step_with<T, C, EPI, NORM>(s, i, a, b, o, x, y);
-      if (EPI == EPI_RESIDUAL && ep.sumsq_out)
-        ep.sumsq_out[(int64_t)m * groups + head * 4 + i] = ss;
-    }
+  for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
+  sum_partials(a, b, slots, w0, w1, HALVES, h, ca, cb, r);
+  if (!s.store) return;
+  if constexpr (EPI == EPI_GATEUP_SILU) {
+    silu_mul16<NORM>(a, b, s.inv);
+    store16(out + (int64_t)m * out_stride + (int64_t)nt * HEAD + 16 * p, a);
+  } else {
+    const float ss = apply_step_with<T, C, EPI, NORM>(s, i, a, b, o, x, y);
+    if (EPI == EPI_RESIDUAL && ep.sumsq_out)
+      ep.sumsq_out[(int64_t)m * (ep.n_cols / SUMSQ_GROUP) + head * 4 + i] = ss;
   }
 }
 
@@ -648,6 +637,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int64_t u_begin = streams ? sp.start(worker) : 0;
   const int64_t u_end = streams ? sp.start(worker + 1) : 0;
   const Walk walk0{worker, t_stop, (int64_t)workers, u_begin, u_end, k_blocks};
+  // at most 32 rows (single CTAs): shared tiles are finished by their last
+  // contributor instead of after a grid barrier
+  const bool decode = !PAIR && num_tokens <= 32;
+  int* tile_counters = counters + kTileCounterOffset;
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
@@ -662,6 +655,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     tc::mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
+    ctl->nfin = 0;
     tc::fence_barrier_init();
   }
   if (warp == EPI_WARPS && lane == 0) {
@@ -827,7 +821,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                              (static_cast<uint32_t>(quarter * 32) << 16);
       if (!whole) {
         // a shared stream-K tile: publish this CTA's partial (finished in the
-        // second phase)
+        // second phase, or by the tile's last contributor for decode sizes)
         store_partial(taddr, const_cast<float*>(slot_of(slots, cta, kb0 == 0)), hh, row, valid);
       } else if constexpr (EPI == EPI_GATEUP_SILU) {
         T* o = out + (int64_t)(valid ? m : 0) * out_stride + (int64_t)nt * HEAD;
@@ -849,18 +843,57 @@ __global__ void __launch_bounds__(THREADS, 1)
         else
           tc::mbar_arrive(&ctl->tmem_empty[b]);
       }
+      if (!PAIR && !whole && decode) {
+        // Decode sizes: the tile's last contributor finishes it, after its
+        // walk (below), so no CTA waits.  All epilogue threads' partial
+        // stores are ordered before thread 0's fence by the barrier; the
+        // fences release and then acquire the partials.
+        const int64_t tile_u0 = (t - t_stop) * k_blocks;
+        const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + k_blocks - 1);
+        epi_sync();
+        if (threadIdx.x == 0) {
+          __threadfence();
+          if (atomicAdd(&tile_counters[t], 1) == c1 - c0) {
+            tile_counters[t] = 0;  // re-armed for the next call
+            __threadfence();
+            if (ctl->nfin < 4) ctl->fin[ctl->nfin++] = (int)t;
+          }
+        }
+      }
     }
     if (sp.units > 0) {
-      // Second phase (same for every CTA: it depends on the shape only).  A
-      // CTA arrives even after a fault, so the others do not wait it out.
+      // Second phase (same for every CTA: it depends on the shape only).
+      // Decode sizes: the shared tiles this CTA contributed to last, its 8
+      // warps one column pair each (rows 0-31).  Otherwise every CTA meets
+      // at the grid barrier (arriving even after a fault, so the others do
+      // not wait it out) and takes a share of all shared tiles' pieces.
       epi_sync();
-      if (threadIdx.x == 0) ctl->ready = grid_barrier(counters, gridDim.x, ctl);
-      epi_sync();
-      if (*reinterpret_cast<volatile int*>(&ctl->ready) != 0)
-        finish_shared_tiles<T, C, EPI, NORM, PAIR>(slots, sp, t_stop, n_all, n_tiles, out,
-                                                   out_stride, ep, num_tokens, warp, lane);
-      else
-        raise_fault(ctl, fault);
+      bool go = true;
+      if (PAIR || !decode) {
+        if (threadIdx.x == 0) ctl->ready = grid_barrier(counters, gridDim.x, ctl);
+        epi_sync();
+        go = *reinterpret_cast<volatile int*>(&ctl->ready) != 0;
+        if (!go) raise_fault(ctl, fault);
+      }
+      constexpr int HALVES = PAIR ? 2 : 1;  // 128-row halves of a tile
+      const bool spread = PAIR || !decode;
+      const int64_t items = spread ? (n_all - t_stop) * 32 * HALVES
+                                   : *reinterpret_cast<volatile int*>(&ctl->nfin);
+      const int64_t first = spread ? (int64_t)blockIdx.x * EPI_WARPS + warp : 0;
+      const int64_t step = spread ? (int64_t)gridDim.x * EPI_WARPS : 1;
+#pragma unroll 1
+      for (int64_t it = first; go && it < items; it += step) {
+        const int64_t tp = spread ? t_stop + it / (32 * HALVES)
+                                  : *reinterpret_cast<volatile int*>(&ctl->fin[it]);
+        const int h = PAIR ? (int)(it / 32) & 1 : 0;
+        const int p = spread ? (int)(it % 32) >> 2 : warp, g = spread ? (int)(it & 3) : 0;
+        const int64_t tile_u0 = (tp - t_stop) * k_blocks;
+        const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + k_blocks - 1);
+        const int m0p = (int)(tp / n_tiles) * PM + h * BM;
+        if (c0 == c1 || m0p + 32 * g >= num_tokens) continue;  // whole, or no rows here
+        finish_piece<T, C, EPI, NORM, PAIR>(slots, c0, c1, m0p, (int)(tp % n_tiles), p, g, h,
+                                            out, out_stride, ep, num_tokens, lane);
+      }
     }
   }
 
@@ -878,9 +911,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---------------------------------------------------------------- host ----
 // Workspace layout: 2 partial slots per SM (a fixed size for the device),
-// then the grid barrier, in an area of one int32 per 128-row tile.  The
-// barrier sits at the same offset for every shape, so a workspace that a call
-// of one shape left valid serves a call of any other shape that fits in it.
+// then 256 bytes for the grid barrier, then one int32 counter per 128-row
+// tile (decode sizes).  Both sit at offsets that do not depend on the shape
+// and are left zero (the barrier's generation aside), so a workspace that a
+// call of one shape left valid serves a call of any other shape that fits.
 struct QkvShape {
   int m_tiles, n_tiles, k_blocks, ctas;
   bool pair;  // 256-row tiles on CTA pairs (m_tiles counts those)
@@ -901,7 +935,7 @@ QkvShape qkv_shape(int64_t num_tokens, int64_t hidden_size, int total_heads, int
   s.ctas = (int)((units < workers ? units : workers) * (s.pair ? 2 : 1));
   s.slot_bytes = (size_t)2 * sms * SLOT_FLOATS * sizeof(float);
   s.workspace_bytes =
-      s.slot_bytes +
+      s.slot_bytes + kTileCounterOffset * sizeof(int) +
       ((size_t)ceil_div(num_tokens, BM) * s.n_tiles * sizeof(int) + 255) / 256 * 256;
   return s;
 }
@@ -1337,7 +1371,8 @@ namespace {
 constexpr int kNoAllocCtas = 63;
 constexpr int kNoAllocTiles = 16384;
 constexpr size_t kNoAllocSlotBytes = (size_t)2 * kNoAllocCtas * SLOT_FLOATS * sizeof(float);
-constexpr size_t kNoAllocBytes = kNoAllocSlotBytes + (size_t)kNoAllocTiles * sizeof(int);
+constexpr size_t kNoAllocBytes =
+    kNoAllocSlotBytes + (size_t)(kTileCounterOffset + kNoAllocTiles) * sizeof(int);
 constexpr int kMaxDevices = 64;
 }  // namespace
 }  // namespace pace
@@ -1423,10 +1458,11 @@ extern "C" int pace_qkv_proj_rope_no_alloc(
   const int cap = sh.pair ? kNoAllocCtas / 2 * 2 : kNoAllocCtas;
   if (sh.ctas > cap) sh.ctas = cap;
   sh.slot_bytes = kNoAllocSlotBytes;
-  // The counters must start at zero.  Calls leave them zero, but one whose
-  // wait expired may not: clear them on the stream first (no allocation).
+  // The barrier and tile counters must start at zero.  Calls leave them zero,
+  // but one whose wait expired may not: clear them on the stream first (no
+  // allocation).
   cudaError_t err = cudaMemsetAsync(static_cast<char*>(scratch) + kNoAllocSlotBytes, 0,
-                                    (size_t)tiles * sizeof(int), stream);
+                                    (size_t)(kTileCounterOffset + tiles) * sizeof(int), stream);
   if (err != cudaSuccess) return cuda_fail(err, name);
   const bool bf16 = dtype == PACE_BF16;
   CUtensorMap ma, mb;

@@ -179,12 +179,14 @@ def test_c_abi_direct_call_and_workspace_reuse():
         assert st == cabi.PACE_OK, lib.pace_last_error()
         torch.cuda.synchronize()
         check(out, ref, torch.bfloat16)
-    # the grid barrier at the end of the workspace: arrival count re-armed,
-    # one generation per call that needed it (none when the tiles run
-    # data-parallel), nothing else written
-    bar = ws[-256:].view(torch.int32)
+    # after the partial slots (two of 128 x 256 fp32 per SM): the grid barrier
+    # (arrival count re-armed, one generation per call that needed it, none
+    # when the tiles run data-parallel), then the per-tile counters, all zero
+    slot_bytes = 2 * torch.cuda.get_device_properties(0).multi_processor_count * 128 * 256 * 4
+    bar = ws[slot_bytes: slot_bytes + 256].view(torch.int32)
     assert bar[0].item() == 0 and bar[32].item() in (0, 3)
     assert int(bar[1:32].sum().item()) == 0 and int(bar[33:].sum().item()) == 0
+    assert int(ws[slot_bytes + 256:].sum().item()) == 0
     st = lib.pace_qkv_proj_rope(out.data_ptr(), hd_.data_ptr(), wd.data_ptr(), pd.data_ptr(), T,
                                 H, nq, nkv, hd, H, n, cd.data_ptr(), cabi.PACE_F32, hd, 8192, 1,
                                 cabi.PACE_BF16, ws.data_ptr(), need - 1, None, stream)
