@@ -482,6 +482,19 @@ __device__ __forceinline__ void finish_gateup_tmem(uint32_t taddr, int half, T* 
 // line, so the waiters' polls do not contend with the arrivals) that the
 // others wait on (bounded).  The whole grid is co-resident (at most one CTA
 // per SM, grid <= SMs or resident CTA pairs), so every CTA arrives.
+// Arrival on a counter: a gpu-scope acquire-release add, so the caller's
+// earlier writes (and those of the threads ordered before it by a CTA
+// barrier) are released with the arrival, and an arriver that sees the
+// final count has acquired every earlier arriver's writes.
+__device__ __forceinline__ int arrive_acq_rel(int* counter) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+               : "=r"(old)
+               : "l"(counter)
+               : "memory");
+  return old;
+}
+
 constexpr int kGenOffset = 32;
 // Per-tile arrival counters (decode sizes) start after the barrier's 256 bytes.
 constexpr int kTileCounterOffset = 64;
@@ -489,10 +502,8 @@ __device__ __forceinline__ bool grid_barrier(int* bar, int ctas, const Ctl* ctl)
   int* gen = bar + kGenOffset;
   int gen0;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(gen0) : "l"(gen) : "memory");
-  __threadfence();  // release the CTA's partials before its arrival
-  if (atomicAdd(bar, 1) == ctas - 1) {
+  if (arrive_acq_rel(bar) == ctas - 1) {
     *reinterpret_cast<volatile int*>(bar) = 0;  // re-armed for the next call
-    __threadfence();  // acquire the other CTAs' arrivals (and their partials)
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(gen), "r"(gen0 + 1) : "memory");
     return true;
   }
@@ -561,10 +572,24 @@ __device__ __forceinline__ void sum_partials(float* va, float* vb, const float* 
 template <typename T, typename C, int EPI, bool NORM, bool PAIR>
 __device__ __forceinline__ void finish_piece(const float* slots, int w0, int w1, int m0, int nt,
                                              int p, int g, int h, T* out, int64_t out_stride,
-                                             const EpiParams& ep, int num_tokens, int lane) {
+                                             const EpiParams& ep, int num_tokens, int lane,
+                                             bool decode) {
   constexpr int HALVES = PAIR ? 2 : 1;
-  const int r = 32 * g + lane, m = m0 + r;
-  if (m >= num_tokens) return;
+  // Decode sizes (g == 0, at most 32 rows): the warp's lanes split into
+  // groups of R >= rows lanes; group k sums workers w0 + k, w0 + k + groups,
+  // ... for its rows, and the groups are added in a fixed tree, so a few
+  // rows with many contributors cost one round of loads, not one per
+  // contributor.  Otherwise a lane takes one row and every worker.
+  int rows_here = 32, R = 32;
+  if (decode) {
+    rows_here = min(32, num_tokens - m0);
+    R = 1;
+    while (R < rows_here) R <<= 1;
+  }
+  const int grp = lane / R, groups = 32 / R;
+  const int r = 32 * g + lane % R, m = m0 + r;
+  const bool row_ok = m < num_tokens && lane % R < rows_here;
+  if (!decode && !row_ok) return;
   int ca, cb, head, i;
   if (EPI == EPI_GATEUP_SILU) {
     ca = p, cb = 8 + p, head = 0, i = 0;
@@ -579,14 +604,46 @@ __device__ __forceinline__ void finish_piece(const float* slots, int w0, int w1,
   // residual values) are requested before and between the partial loads,
   // so their latencies overlap; a head past the output (odd head counts)
   // only skips the store.
-  const RowState<C> s = row_state<C, EPI, NORM>(ep, m, true, head);
+  const RowState<C> s = row_state<C, EPI, NORM>(ep, row_ok ? m : m0, row_ok, head);
   T* o = out + (int64_t)m * out_stride + (int64_t)head * HEAD;
   float x[16], y[16];
-  if constexpr (EPI != EPI_GATEUP_SILU) load_step_inputs<T, C, EPI>(s, i, o, x, y);
+  if constexpr (EPI != EPI_GATEUP_SILU) {
+    if (grp == 0) load_step_inputs<T, C, EPI>(s, i, o, x, y);
+  }
   float a[16], b[16];
 #pragma unroll
   for (int e = 0; e < 16; ++e) a[e] = b[e] = 0.f;
-  sum_partials(a, b, slots, w0, w1, HALVES, h, ca, cb, r);
+  if (!decode) {
+    sum_partials(a, b, slots, w0, w1, HALVES, h, ca, cb, r);
+  } else {
+    if (row_ok) {
+#pragma unroll 1
+      for (int w = w0 + grp; w <= w1; w += groups) {
+        float* sl = const_cast<float*>(slot_of(slots, w * HALVES + h, w == w0));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 fa = ld_cg_f4(slot_q(sl, ca, q, r));
+          const float4 fb = ld_cg_f4(slot_q(sl, cb, q, r));
+          a[4 * q] += fa.x;
+          a[4 * q + 1] += fa.y;
+          a[4 * q + 2] += fa.z;
+          a[4 * q + 3] += fa.w;
+          b[4 * q] += fb.x;
+          b[4 * q + 1] += fb.y;
+          b[4 * q + 2] += fb.z;
+          b[4 * q + 3] += fb.w;
+        }
+      }
+    }
+    for (int off = 16; off >= R; off >>= 1) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        a[e] += __shfl_down_sync(0xffffffffu, a[e], off);
+        b[e] += __shfl_down_sync(0xffffffffu, b[e], off);
+      }
+    }
+    if (grp != 0 || !row_ok) return;
+  }
   if (!s.store) return;
   if constexpr (EPI == EPI_GATEUP_SILU) {
     silu_mul16<NORM>(a, b, s.inv);
@@ -846,18 +903,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!PAIR && !whole && decode) {
         // Decode sizes: the tile's last contributor finishes it, after its
         // walk (below), so no CTA waits.  All epilogue threads' partial
-        // stores are ordered before thread 0's fence by the barrier; the
-        // fences release and then acquire the partials.
+        // stores are ordered before thread 0's arrival by the barrier.
         const int64_t tile_u0 = (t - t_stop) * k_blocks;
         const int c0 = sp.owner(tile_u0), c1 = sp.owner(tile_u0 + k_blocks - 1);
         epi_sync();
-        if (threadIdx.x == 0) {
-          __threadfence();
-          if (atomicAdd(&tile_counters[t], 1) == c1 - c0) {
-            tile_counters[t] = 0;  // re-armed for the next call
-            __threadfence();
-            if (ctl->nfin < 4) ctl->fin[ctl->nfin++] = (int)t;
-          }
+        if (threadIdx.x == 0 && arrive_acq_rel(&tile_counters[t]) == c1 - c0) {
+          tile_counters[t] = 0;  // re-armed for the next call
+          if (ctl->nfin < 4) ctl->fin[ctl->nfin++] = (int)t;
         }
       }
     }
@@ -892,7 +944,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int m0p = (int)(tp / n_tiles) * PM + h * BM;
         if (c0 == c1 || m0p + 32 * g >= num_tokens) continue;  // whole, or no rows here
         finish_piece<T, C, EPI, NORM, PAIR>(slots, c0, c1, m0p, (int)(tp % n_tiles), p, g, h,
-                                            out, out_stride, ep, num_tokens, lane);
+                                            out, out_stride, ep, num_tokens, lane, !spread);
       }
     }
   }
