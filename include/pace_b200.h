@@ -101,13 +101,15 @@ int pace_rotary_embedding(const int64_t* positions, void* query, void* key, int6
  * workspace: device memory of at least pace_qkv_proj_rope_workspace_size()
  * bytes (for this shape and device), 256-byte aligned, ZERO-FILLED before its
  * first use; every call leaves it valid for the next (its grid-barrier count
- * back at zero, at an offset that does not depend on the shape), so one
- * zeroed workspace serves any number of stream-ordered calls of any shapes
- * that fit in it.  Calls that may run concurrently need separate workspaces.
- * The kernel's CTAs (at most one per SM) meet at one grid-wide barrier, so
- * they must all be resident together: the call sizes its grid by the
- * device's SM count, and a context limited to fewer SMs (an MPS share, a
- * green context) sees the bounded wait expire instead.
+ * and per-tile counters back at zero, at offsets that do not depend on the
+ * shape), so one zeroed workspace serves any number of stream-ordered calls
+ * of any shapes that fit in it.  Calls that may run concurrently need
+ * separate workspaces.  Above 32 tokens the kernel's CTAs (at most one per
+ * SM) may meet at one grid-wide barrier, so they must all be resident
+ * together: the call sizes its grid by the device's SM count (clusters of
+ * two above 128 tokens, by cudaOccupancyMaxActiveClusters), and a context
+ * limited to fewer SMs (an MPS share, a green context) sees the bounded wait
+ * expire instead.
  * fault_flags (optional device int32, may be NULL): bit 30 is OR-ed in when a
  * bounded device wait expires (the output is then incomplete and the
  * workspace must be zero-filled again before reuse).
