@@ -1,38 +1,44 @@
-// Fused qkv projection + rotary embedding for sm_100a (tcgen05 tensor cores).
+// GEMMs with the layer's elementwise work in their epilogues, for sm_100a
+// (tcgen05 tensor cores): out = epilogue(A @ W^T), A [T, K] rows, W [N, K].
 //
-// Replaces the pair qkv_proj -> rotary_emb of LlamaAttention.forward
-// (paceserve/model_executor/models/llama.py:176-178): the projection
-// qkv = hidden @ W_qkv^T (F.linear, a library GEMM in the reference) followed
-// by the in-place rotary embedding of the q and k columns
-// (csrc/pos_encoding_kernels.cu:38-76, cache row = [cos(rot/2) | sin(rot/2)]).
-// Here the rotation is applied to the fp32 accumulator in the GEMM's epilogue,
-// so the q/k values are rounded to the storage type once (the unfused path
-// rounds the GEMM output, then rotates and rounds again) and the separate rope
-// launch and its 4(nq+nkv)hd bytes per token of HBM traffic disappear.
+// Epilogues (each replaces a reference op that would run after the GEMM):
+//  * rope: the qkv projection followed by the in-place rotary embedding of
+//    the q and k heads (paceserve/model_executor/models/llama.py:176-178,
+//    csrc/pos_encoding_kernels.cu:38-76; cache row = [cos(rot/2) | sin(rot/2)]),
+//    applied to the fp32 accumulator, so q/k are rounded once and the rope
+//    launch and its 4 (nq + nkv) hd bytes per token disappear;
+//  * rope with the input RMSNorm as a per-row factor (norm weight folded into
+//    W, the row statistics written by the GEMM before);
+//  * residual: o_proj / down_proj plus the residual add, writing the new
+//    rows' sum of squares per 32 columns for the next norm;
+//  * gate/up: silu(gate) * up from a tile holding 128 gate and the matching
+//    128 up columns (W = [gate rows; up rows], llama.py:70-104), optionally
+//    with the post-attention RMSNorm factor.
 //
-// Work decomposition (stream-K): the output is cut into 128 x 256 tiles (two
-// heads, so both halves of every NeoX pair (i, i + 64) and every GPT-J pair
-// (2i, 2i + 1) of a head sit in one tile), each tile into 64-element K blocks,
-// and the (tile, K block) units are split evenly over one persistent CTA per
-// SM.  A CTA whose range covers a whole tile finishes it directly from TMEM.
-// Every other segment belongs to a tile shared by consecutive CTAs; its CTA
-// stores the fp32 partial sum in the caller's workspace.  When all CTAs have
-// stored theirs (one grid-wide barrier: the grid, at most one CTA per SM, is
-// co-resident, and the wait is bounded), every epilogue warp of the grid
-// takes a share of the shared tiles' (column pair, 32 rows) pieces, adds the
-// contributors' partials in CTA order (so the result does not depend on
-// timing), applies the epilogue and stores.  Spreading that reduction over
-// all SMs, instead of leaving each tile to one CTA, is what keeps decode-size
-// calls (T <= 128, six contributors per tile) short.  At T=512 this gives
-// every SM 41.5 units instead of one or two whole tiles.
+// Tiles are 128 rows x 256 accumulator columns (for rope two whole heads, so
+// both halves of every NeoX pair (i, i + 64) and every GPT-J pair (2i, 2i + 1)
+// sit in one tile), or 256 rows on a CTA pair (PAIR, T > 128: a two-CTA
+// cluster sharing cta_group::2 MMAs, each CTA holding its 128 rows and half
+// of B), in 64-element K blocks.  The workers (CTAs or pairs, one per SM or
+// SM pair, persistent) take whole tiles round-robin, then either one more
+// data-parallel round on fewer workers or a stream-K split of the leftover
+// tiles' (tile, K block) units over all of them (schedule_workers).  A
+// segment that covers a whole tile is finished from TMEM.  Any other stores
+// its fp32 partial in the caller's workspace, and the tile is finished later
+// from the partials, added in worker order so the result does not depend on
+// timing: at decode sizes (<= 32 rows) by its last contributor (a per-tile
+// counter; no CTA waits), otherwise after one grid-wide barrier by all
+// epilogue warps of the grid, a (column pair, 32 rows) piece each.  The grid
+// is co-resident (at most one CTA per SM) and every wait is bounded.
 //
-// Inside a CTA: a 4-stage shared-memory ring of A (128 x 64) and B (256 x 64)
-// blocks filled by TMA (128-byte swizzle, no multicast; warp 8), tcgen05.mma
-// (M=128, N=256, K=16, fp32) issued by one thread of warp 9 into one of two
-// 256-column TMEM accumulators, and 8 epilogue warps (warp w owns TMEM lanes
-// 32(w % 4)..+31, i.e. tile rows, and head w / 4 of the tile) that drain one
-// accumulator while the MMAs fill the other.  Every mbarrier wait is bounded by %globaltimer; on expiry the
-// CTA records bit 30 in the caller's fault word, stops issuing, waits (bounded
+// Inside a CTA: a shared-memory ring of A (128 x 64) and B (256 or, PAIR,
+// 128 x 64) blocks filled by TMA (128-byte swizzle, no multicast; warp 8),
+// tcgen05.mma (M=128 or 256, N=256, K=16, fp32) issued by one thread of warp 9
+// (of the pair leader) into one of two 256-column TMEM accumulators, and 8
+// epilogue warps (warp w owns TMEM lanes 32(w % 4)..+31, i.e. tile rows, and
+// head w / 4 of the tile) that drain one accumulator while the MMAs fill the
+// other.  Every mbarrier wait is bounded by %globaltimer; on expiry the CTA
+// records bit 30 in the caller's fault word, stops issuing, waits (bounded
 // again) for its own copies and MMAs, frees TMEM and returns.
 #include <mutex>
 
