@@ -58,7 +58,7 @@ def test_linear_residual_and_row_sumsq(T, K, N):
     assert torch.allclose(ss2.cpu().double(), want_ss, rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("T", [1, 64, 512])
+@pytest.mark.parametrize("T", [1, 64, 256, 512])
 @pytest.mark.parametrize("neox", [True, False])
 def test_qkv_proj_rmsnorm_rope(T, neox):
     nq, nkv, hd, H = 32, 8, 128, 4096

@@ -53,9 +53,12 @@ def check(got, ref, dtype, tight=True):
         assert ((g - r).abs() <= bound).all(), ((g - r).abs() - bound).max().item()
 
 
-@pytest.mark.parametrize("T", [1, 17, 128, 300, 512])
+@pytest.mark.parametrize("T", [1, 17, 128, 200, 256, 300, 512])
 @pytest.mark.parametrize("neox", [True, False])
 def test_llama3_8b_shape(T, neox):
+    # T <= 128: single CTAs (T = 1 and 17 finish shared tiles by their last
+    # contributor); T = 200 and 256: CTA pairs, stream-K; 300 and 512: CTA
+    # pairs, one data-parallel round
     nq, nkv, hd, H = 32, 8, 128, 4096
     hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, T)
     qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
