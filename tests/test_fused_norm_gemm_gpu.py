@@ -58,6 +58,26 @@ def test_linear_residual_and_row_sumsq(T, K, N):
     assert torch.allclose(ss2.cpu().double(), want_ss, rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("T", [20, 300])
+def test_linear_residual_float16_strided_rows_without_sumsq(T):
+    """fp16 rounding of the residual add; input and residual as column slices
+    of wider rows; no sum-of-squares output.  T=20 finishes shared stream-K
+    tiles by their last contributor, T=300 runs on CTA pairs."""
+    K, N = 2048, 1024
+    g = torch.Generator().manual_seed(T + 1)
+    a_wide = rnd((T, K + 64), g, dtype=torch.float16).to(DEV)
+    a = a_wide[:, 64:]
+    w = rnd((N, K), g, K ** -0.5, dtype=torch.float16).to(DEV)
+    res_wide = rnd((T, N + 128), g, dtype=torch.float16).to(DEV)
+    res = res_wide[:, :N]
+    tail = res_wide[:, N:].clone()
+    ref = res.float().cpu() + a.float().cpu() @ w.float().cpu().t()
+    layernorm_ops.linear_residual(res, a, w)
+    torch.cuda.synchronize()
+    close(res, ref, torch.float16)
+    assert torch.equal(res_wide[:, N:], tail)  # nothing written past the row
+
+
 @pytest.mark.parametrize("T", [1, 64, 256, 512])
 @pytest.mark.parametrize("neox", [True, False])
 def test_qkv_proj_rmsnorm_rope(T, neox):
