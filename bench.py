@@ -331,7 +331,8 @@ def e2e_chain(chs, ops, steps, warmup, ws=1):
     """Public-API path, pipelined the way a serving engine runs it: step i uses chain
     state i % 2 (`chs` holds two); its inputs go host -> device on an H2D stream
     from page-locked memory, the ops run eagerly (pybind -> C ABI) on the compute
-    stream, and its output goes device -> host on a D2H stream, so the copies of
+    stream, and its result -- the last layer's residual stream [T, H], what a layer
+    hands to the next -- goes device -> host on a D2H stream, so the copies of
     one step overlap the ops of the next.  Events order every reuse of a buffer.
     Every step's copies lie inside the timed region.  With ws > 1 every rank runs
     it between barriers; the time is the max over ranks and the value the whole
@@ -343,7 +344,7 @@ def e2e_chain(chs, ops, steps, warmup, ws=1):
     h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
     h_pos = [c["positions"].cpu().pin_memory() for c in chs]
     h_hidden = [c["layers"][0]["hidden"].cpu().pin_memory() for c in chs]
-    h_out = [torch.empty(T, I, dtype=torch.bfloat16, pin_memory=True) for _ in chs]
+    h_out = [torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True) for _ in chs]
     comp_done = [torch.cuda.Event() for _ in chs]
     d2h_done = [torch.cuda.Event() for _ in chs]
     for e in comp_done + d2h_done:
@@ -364,7 +365,7 @@ def e2e_chain(chs, ops, steps, warmup, ws=1):
         comp_done[k].record(comp)
         with torch.cuda.stream(d2h_s):
             d2h_s.wait_event(comp_done[k])
-            h_out[k].copy_(ch["layers"][-1]["act"], non_blocking=True)
+            h_out[k].copy_(ch["layers"][-1]["residual2"], non_blocking=True)
             d2h_done[k].record(d2h_s)
 
     for i in range(warmup):
@@ -396,8 +397,8 @@ def e2e_chain(chs, ops, steps, warmup, ws=1):
             "d2h_bytes_per_step": h_out[0].numel() * 2, "ms_per_step": round(ms, 4),
             "steps": steps,
             "path": "eager calls of paceserve_b200 ops (pybind -> C ABI); inputs in and the "
-                    "last layer's output out every step, on copy streams overlapping the "
-                    "next step's ops"}
+                    "last layer's residual stream out every step, on copy streams "
+                    "overlapping the next step's ops"}
 
 
 def e2e_breakdown(chs, ops, steps, warmup, ws=1):
@@ -412,7 +413,7 @@ def e2e_breakdown(chs, ops, steps, warmup, ws=1):
     h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
     h_pos = [c["positions"].cpu().pin_memory() for c in chs]
     h_hidden = [c["layers"][0]["hidden"].cpu().pin_memory() for c in chs]
-    h_out = [torch.empty(T, I, dtype=torch.bfloat16, pin_memory=True) for _ in chs]
+    h_out = [torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True) for _ in chs]
 
     def timed(step):
         for i in range(warmup):
@@ -452,7 +453,7 @@ def e2e_breakdown(chs, ops, steps, warmup, ws=1):
             chs[k]["positions"].copy_(h_pos[k], non_blocking=True)
             chs[k]["layers"][0]["hidden"].copy_(h_hidden[k], non_blocking=True)
         with torch.cuda.stream(d2h_s):
-            h_out[k].copy_(chs[k]["layers"][-1]["act"], non_blocking=True)
+            h_out[k].copy_(chs[k]["layers"][-1]["residual2"], non_blocking=True)
 
     ms_l, host_l = timed(launches)
     ms_c, _ = timed(copies)
