@@ -1150,9 +1150,10 @@ def moe_routing(dev, reps=50):
     return out
 
 
-def qkv_rope_bench(dev, tokens=(1, 128, 512, 2048), reps=10):
+def qkv_rope_bench(dev, tokens=(1, 2, 128, 512, 2048), reps=10):
     """The fused qkv projection + rotary embedding (tcgen05 GEMM, rope in the
-    epilogue) against the path it replaces: cuBLAS (torch.matmul) for the
+    epilogue; at most 2 tokens, the weight-streaming CUDA-core kernel) against
+    the path it replaces: cuBLAS (torch.matmul) for the
     projection, then the rotary_embedding op on the q/k views.  Llama-3-8B
     (hidden 4096 -> 6144 = 32 q + 8 k + 8 v heads of 128), bf16, fp32 cache,
     positions as the Sarathi batch draws them.  Each variant is a CUDA graph
@@ -1176,11 +1177,16 @@ def qkv_rope_bench(dev, tokens=(1, 128, 512, 2048), reps=10):
         pos = torch.randint(0, MAX_POS, (t,), generator=g_, device=dev)
         outs = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
         refs = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        # the caller's zeroed workspace (none needed at decode sizes), so no
+        # capture records the shim allocating and zero-filling its own
+        need = pb.pos_encoding_ops.qkv_proj_rope_workspace_size(t, H, nq, nkv,
+                                                                torch.device(dev).index or 0)
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev) if need else None
 
         def fused():
             for x, w, o in zip(xs, weights, outs):
                 pb.pos_encoding_ops.qkv_proj_rotary_embedding(o, x, w, pos, HD, nq, nkv, cache,
-                                                              True)
+                                                              True, None, ws)
 
         def gemm():
             for x, w, o in zip(xs, weights, refs):
@@ -1196,7 +1202,7 @@ def qkv_rope_bench(dev, tokens=(1, 128, 512, 2048), reps=10):
         res = {"T": t}
         for name, fn in (("fused_us", fused), ("cublas_gemm_us", gemm),
                          ("cublas_gemm_plus_rope_us", unfused)):
-            fn()  # eager once (the shim's workspace is allocated outside capture)
+            fn()  # eager once
             gr = capture(fn)
             res[name] = round(time_replays(gr, reps, 3) * 1e3 / (reps * nbuf), 3)
             del gr
@@ -1739,7 +1745,8 @@ def main():
                        "rows": moe_routing(dev, reps=50)}
         torch.cuda.empty_cache()
         line["qkv_rope"] = {"what": "fused qkv projection + rotary embedding (tcgen05 GEMM, rope in "
-                                    "the epilogue) vs cuBLAS GEMM then the rope op; Llama-3-8B "
+                                    "the epilogue; at most 2 tokens: a weight-streaming kernel on "
+                                    "CUDA cores) vs cuBLAS GEMM then the rope op; Llama-3-8B "
                                     "4096 -> 6144, bf16, 4 weight buffers per graph (> L2)",
                             "peak_tflops": pk["bf16_tflops"], "rows": qkv_rope_bench(dev)}
         torch.cuda.empty_cache()

@@ -98,6 +98,11 @@ int pace_rotary_embedding(const int64_t* positions, void* query, void* key, int6
  * rot_dim = 128; hidden_size and both row strides multiples of 8 elements;
  * qkv_out, hidden, weight and the cache 16-byte aligned.  Tokens whose
  * position lies outside [0, max_position) are stored unrotated.
+ * Up to 2 tokens (decode batches) the projection runs on the CUDA cores
+ * instead: a stream of the weight through shared memory, one warp per
+ * rotation pair of output columns over the whole K, the same epilogue; it
+ * needs no workspace (pace_qkv_proj_rope_workspace_size returns 0, and
+ * workspace may be NULL).
  * workspace: device memory of at least pace_qkv_proj_rope_workspace_size()
  * bytes (for this shape and device), 256-byte aligned, ZERO-FILLED before its
  * first use; every call leaves it valid for the next (its grid-barrier count
@@ -147,7 +152,8 @@ int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
  *   the caller.  Equal to rms_norm then the projection up to the rounding of
  *   the normalised rows (the reference rounds them to T before its GEMM).
  *   row_sumsq 16-byte aligned, sumsq_groups (= hidden_size / 32) a multiple
- *   of 4.
+ *   of 4.  Up to 2 tokens it runs on the CUDA cores without a workspace, as
+ *   pace_qkv_proj_rope does.
  * Replace fused_add_rms_norm + qkv_proj (llama.py:176, 240-254) and the
  * residual add after o_proj / the MLP.  No reference kernel. */
 size_t pace_linear_residual_workspace_size(int64_t num_tokens, int64_t n, int64_t k, int device);

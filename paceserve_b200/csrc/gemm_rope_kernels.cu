@@ -40,6 +40,8 @@
 // other.  Every mbarrier wait is bounded by %globaltimer; on expiry the CTA
 // records bit 30 in the caller's fault word, stops issuing, waits (bounded
 // again) for its own copies and MMAs, frees TMEM and returns.
+#include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "tcgen05.cuh"
@@ -967,6 +969,233 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ------------------------------------------ decode batches on CUDA cores --
+// With at most kGemvTokens rows the projection is a stream of the weight
+// (50 MB for Llama-3-8B's qkv) past a few hidden rows: HBM-bound, with a
+// 128-row MMA tile almost all padding and the split-K reduction that the tile
+// schedule needs at this size costing more than the stream itself.  A CTA
+// owns up to kGemvPairs rotation pairs of output columns (NeoX: head columns
+// i and i + 64; GPT-J: 2i and 2i + 1) over the whole K, so no sum crosses
+// CTAs; the pairs are spread evenly over three CTAs per SM.  One producer
+// thread streams the pairs' weight rows through a ring of kGemvStages
+// shared-memory stages with bulk copies (kGemvChunk elements of every row per
+// stage, 64 KB in flight per CTA: register loads could not keep enough bytes
+// in flight to cover the DRAM latency).  Consumer warp j copies pair j's two
+// row chunks to registers, releases the stage, and dots them with the hidden
+// rows (read through L1, which the CTA's warps share); after the last chunk it
+// reduces across the warp, and lane t finishes token t as the tensor-core
+// epilogue does: norm factor, rotation in fp32, one rounding.  Every wait is
+// bounded; on expiry the CTA sets bit 30 of the fault word, stops, and the
+// producer waits (bounded) for its copies before leaving.
+constexpr int kGemvTokens = 2, kGemvPairs = 8, kGemvChunk = 512, kGemvStages = 4;
+constexpr int kGemvStageElems = 2 * kGemvPairs * kGemvChunk;  // 16-bit weights
+constexpr int kGemvThreads = (kGemvPairs + 1) * 32;
+constexpr int kGemvVec = kGemvChunk / 256;  // 16-byte vectors per lane, row and chunk
+struct GemvCtl {
+  uint64_t full[kGemvStages], empty[kGemvStages];
+  int abort;
+};
+constexpr int kGemvSmem = kGemvStages * kGemvStageElems * 2 + (int)sizeof(GemvCtl);
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Plain (non-multicast) bulk copy global -> this CTA's shared memory,
+// completing `bytes` of transaction count on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          tc::smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+template <bool NEOX>
+__device__ __forceinline__ void pair_columns(int unit, int& head, int& i, int& c1, int& c2) {
+  head = unit / (HEAD / 2);
+  i = unit % (HEAD / 2);
+  c1 = head * HEAD + (NEOX ? i : 2 * i);
+  c2 = c1 + (NEOX ? HEAD / 2 : 1);
+}
+
+// NT: tokens the loops are unrolled for (num_tokens <= NT).  Measured on
+// B200 (Llama-3-8B qkv, 50 MB of weight): 9.8 us at one token, 12.9 at two,
+// against 11.9 for cuBLAS's GEMM alone; from three tokens on the tensor-core
+// kernel is faster, so kGemvTokens is 2.
+template <typename T, typename C, bool NEOX, bool NORM, int NT>
+__global__ void __launch_bounds__(kGemvThreads, 3)
+    gemv_rope_kernel(const T* __restrict__ hidden, int64_t hidden_stride,
+                     const T* __restrict__ weight, int64_t k, T* __restrict__ out,
+                     int64_t out_stride, int num_tokens, const EpiParams ep, int32_t* fault) {
+  extern __shared__ __align__(16) uint8_t gemv_smem[];
+  T* ring = reinterpret_cast<T*>(gemv_smem);
+  GemvCtl* ctl = reinterpret_cast<GemvCtl*>(gemv_smem + kGemvStages * kGemvStageElems * 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = ep.n_cols / 2;
+  const int unit0 = (int)((int64_t)blockIdx.x * units / gridDim.x);
+  const int pairs = (int)((int64_t)(blockIdx.x + 1) * units / gridDim.x) - unit0;
+  const int chunks = (int)ceil_div(k, kGemvChunk);
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemvStages; ++s) {
+      tc::mbar_init(&ctl->full[s], 1);
+      tc::mbar_init(&ctl->empty[s], kGemvPairs);
+    }
+    ctl->abort = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kGemvPairs) {
+    // ---- producer: every chunk of every row of the CTA's pairs ----------
+    if (lane != 0) return;
+    pdl_wait();
+    int c = 0;
+    bool ok = true;
+    for (; c < chunks; ++c) {
+      const int s = c % kGemvStages;
+      if (c >= kGemvStages && !tc::mbar_wait(&ctl->empty[s], (uint32_t)(c / kGemvStages - 1) & 1u,
+                                             kWaitLimitNs, &ctl->abort)) {
+        ok = false;
+        break;
+      }
+      const int64_t k0 = (int64_t)c * kGemvChunk;
+      const uint32_t bytes = (uint32_t)(min((int64_t)kGemvChunk, k - k0) * (int64_t)sizeof(T));
+      tc::mbar_arrive_expect_tx(&ctl->full[s], bytes * 2u * (uint32_t)pairs);
+      T* st = ring + (size_t)s * kGemvStageElems;
+      for (int j = 0; j < pairs; ++j) {
+        int head, i, c1, c2;
+        pair_columns<NEOX>(unit0 + j, head, i, c1, c2);
+        bulk_g2s(st + (2 * j) * kGemvChunk, weight + (int64_t)c1 * k + k0, bytes, &ctl->full[s]);
+        bulk_g2s(st + (2 * j + 1) * kGemvChunk, weight + (int64_t)c2 * k + k0, bytes,
+                 &ctl->full[s]);
+      }
+    }
+    if (!ok) {
+      *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+      if (fault) atomicOr(fault, kFaultTimeout);
+    }
+    // every copy issued has landed before the CTA's shared memory is released
+    for (int q = c > kGemvStages ? c - kGemvStages : 0; q < c; ++q)
+      tc::mbar_wait(&ctl->full[q % kGemvStages], (uint32_t)(q / kGemvStages) & 1u, kWaitLimitNs,
+                    nullptr);
+    return;
+  }
+
+  // ---- consumer warp `warp`: rotation pair unit0 + warp ------------------
+  const bool has = warp < pairs;
+  int head = 0, i = 0, c1 = 0, c2 = 0;
+  if (has) pair_columns<NEOX>(unit0 + warp, head, i, c1, c2);
+  float acc1[NT], acc2[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc1[t] = acc2[t] = 0.f;
+  // the hidden rows (NORM: and their partials) may be written by the previous kernel
+  pdl_wait();
+  bool ok = true;
+  for (int c = 0; c < chunks; ++c) {
+    const int s = c % kGemvStages;
+    const int64_t k0 = (int64_t)c * kGemvChunk;
+    const int nvc = (int)(min((int64_t)kGemvChunk, k - k0) / 8);  // 16-byte vectors per row
+    // this chunk's hidden vectors, issued before the wait on the ring
+    uint4 xv[kGemvVec][NT];
+#pragma unroll
+    for (int q = 0; q < kGemvVec; ++q) {
+      const int v = lane + 32 * q;
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (has && t < num_tokens && v < nvc)
+          xv[q][t] = __ldg(reinterpret_cast<const uint4*>(hidden + t * hidden_stride + k0) + v);
+    }
+    if (!tc::mbar_wait(&ctl->full[s], (uint32_t)(c / kGemvStages) & 1u, kWaitLimitNs,
+                       &ctl->abort)) {
+      ok = false;
+      break;
+    }
+    // the pair's row chunks to registers; the stage is free for the next copy
+    uint4 wa[kGemvVec], wb[kGemvVec];
+    const T* st = ring + (size_t)s * kGemvStageElems;
+#pragma unroll
+    for (int q = 0; q < kGemvVec; ++q) {
+      const int v = lane + 32 * q;
+      if (has && v < nvc) {
+        wa[q] = *reinterpret_cast<const uint4*>(st + (2 * warp) * kGemvChunk + 8 * v);
+        wb[q] = *reinterpret_cast<const uint4*>(st + (2 * warp + 1) * kGemvChunk + 8 * v);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&ctl->empty[s]);
+#pragma unroll
+    for (int q = 0; q < kGemvVec; ++q) {
+      const int v = lane + 32 * q;
+      if (has && v < nvc) {
+        float w1[8], w2[8];
+        Traits<T>::unpack(wa[q], w1);
+        Traits<T>::unpack(wb[q], w2);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          if (t < num_tokens) {
+            float x[8];
+            Traits<T>::unpack(xv[q][t], x);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              acc1[t] = fmaf(w1[e], x[e], acc1[t]);
+              acc2[t] = fmaf(w2[e], x[e], acc2[t]);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (!ok) {
+    *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+    if (fault && lane == 0) atomicOr(fault, kFaultTimeout);
+    return;
+  }
+  if (!has) return;
+  float f[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    acc1[t] = warp_sum(acc1[t]);
+    acc2[t] = warp_sum(acc2[t]);
+    f[t] = 1.f;
+    if (NORM && t < num_tokens) {
+      const float* p = ep.sumsq_in + (int64_t)t * ep.sumsq_in_groups;
+      float ss = 0.f;
+      for (int g = lane; g < ep.sumsq_in_groups; g += 32) ss += __ldg(p + g);
+      f[t] = rsqrtf(warp_sum(ss) * ep.inv_k + ep.eps);
+    }
+  }
+  if (lane >= num_tokens) return;
+  float x1 = 0.f, x2 = 0.f, inv = 1.f;
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    if (t == lane) {
+      x1 = acc1[t];
+      x2 = acc2[t];
+      inv = f[t];
+    }
+  }
+  if (NORM) {
+    x1 *= inv;
+    x2 *= inv;
+  }
+  const int64_t pos = ep.positions[lane];
+  if (head < ep.rot_heads && pos >= 0 && pos < ep.max_position) {
+    const C* cs = static_cast<const C*>(ep.cache) + pos * HEAD;
+    const float cv = Traits<C>::to_f(cs[i]), sv = Traits<C>::to_f(cs[HEAD / 2 + i]);
+    const float y1 = x1 * cv - x2 * sv, y2 = x2 * cv + x1 * sv;
+    x1 = y1;
+    x2 = y2;
+  }
+  T* o = out + (int64_t)lane * out_stride;
+  o[c1] = Traits<T>::from_f(x1);
+  o[c2] = Traits<T>::from_f(x2);
+}
+
 // ---------------------------------------------------------------- host ----
 // Workspace layout: 2 partial slots per SM (a fixed size for the device),
 // then 256 bytes for the grid barrier, then one int32 counter per 128-row
@@ -1097,6 +1326,72 @@ EpiParams rope_params(const int64_t* positions, const void* cache, int64_t max_p
   return ep;
 }
 
+// The decode-batch projection (gemv_rope_kernel) for the dtype pair.
+template <typename T, typename C, bool NEOX, bool NORM, int NT>
+cudaError_t launch_gemv_rope_nt(const void* hidden, int64_t hidden_stride, const void* weight,
+                                int64_t k, void* out, int64_t out_stride, int64_t num_tokens,
+                                const EpiParams& ep, int32_t* fault, int dev,
+                                cudaStream_t stream) {
+  auto kernel = gemv_rope_kernel<T, C, NEOX, NORM, NT>;
+  cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), dev, kGemvSmem);
+  if (err != cudaSuccess) return err;
+  // three CTAs per SM, so the whole grid is resident at once (set once per
+  // kernel and device)
+  static std::atomic<bool> carveout_set[64];
+  if (dev >= 0 && dev < 64 && !carveout_set[dev].load(std::memory_order_acquire)) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    if (err != cudaSuccess) return err;
+    carveout_set[dev].store(true, std::memory_order_release);
+  }
+  // the pairs spread over three CTAs per SM, at most kGemvPairs per CTA
+  const int64_t units = ep.n_cols / 2;
+  const int64_t grid =
+      std::max<int64_t>(ceil_div(units, kGemvPairs), std::min<int64_t>(units, 3 * sm_count(dev)));
+  return launch(kernel, dim3((unsigned)grid), dim3(kGemvThreads), kGemvSmem, stream,
+                static_cast<const T*>(hidden), hidden_stride, static_cast<const T*>(weight), k,
+                static_cast<T*>(out), out_stride, (int)num_tokens, ep, fault);
+}
+
+template <typename T, typename C, bool NEOX, bool NORM>
+cudaError_t launch_gemv_rope_t(const void* hidden, int64_t hidden_stride, const void* weight,
+                               int64_t k, void* out, int64_t out_stride, int64_t num_tokens,
+                               const EpiParams& ep, int32_t* fault, int dev,
+                               cudaStream_t stream) {
+  if (num_tokens == 1)
+    return launch_gemv_rope_nt<T, C, NEOX, NORM, 1>(hidden, hidden_stride, weight, k, out,
+                                                    out_stride, num_tokens, ep, fault, dev, stream);
+  return launch_gemv_rope_nt<T, C, NEOX, NORM, kGemvTokens>(
+      hidden, hidden_stride, weight, k, out, out_stride, num_tokens, ep, fault, dev, stream);
+}
+
+template <bool NORM>
+int launch_gemv_rope(const void* hidden, int64_t hidden_stride, const void* weight, int64_t k,
+                     void* out, int64_t out_stride, int64_t num_tokens, const EpiParams& ep,
+                     int dtype, int cache_dtype, bool neox, int32_t* fault, int dev,
+                     cudaStream_t stream, const char* name) {
+#define PACE_GEMV(T, C, NX)                                                                      \
+  launch_gemv_rope_t<T, C, NX, NORM>(hidden, hidden_stride, weight, k, out, out_stride,          \
+                                     num_tokens, ep, fault, dev, stream)
+  cudaError_t err;
+  const bool f32c = cache_dtype == PACE_F32;
+  if (dtype == PACE_BF16) {
+    if (f32c)
+      err = neox ? PACE_GEMV(__nv_bfloat16, float, true) : PACE_GEMV(__nv_bfloat16, float, false);
+    else
+      err = neox ? PACE_GEMV(__nv_bfloat16, __nv_bfloat16, true)
+                 : PACE_GEMV(__nv_bfloat16, __nv_bfloat16, false);
+  } else {
+    if (f32c)
+      err = neox ? PACE_GEMV(__half, float, true) : PACE_GEMV(__half, float, false);
+    else
+      err = neox ? PACE_GEMV(__half, __half, true) : PACE_GEMV(__half, __half, false);
+  }
+#undef PACE_GEMV
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  return PACE_OK;
+}
+
 template <typename T, typename C, bool NEOX>
 int launch_qkv_rope(const CUtensorMap& ma, const CUtensorMap& mb, void* out, int64_t out_stride,
                     const int64_t* positions, const void* cache, int64_t max_position,
@@ -1118,6 +1413,7 @@ extern "C" size_t pace_qkv_proj_rope_workspace_size(int64_t num_tokens, int64_t 
   if (num_tokens <= 0 || hidden_size <= 0 || num_heads < 0 || num_kv_heads < 0 ||
       num_heads + num_kv_heads <= 0)
     return 0;
+  if (num_tokens <= kGemvTokens) return 0;  // the CUDA-core kernel needs none
   return qkv_shape(num_tokens, hidden_size, num_heads + 2 * num_kv_heads, sm_count(device))
       .workspace_bytes;
 }
@@ -1157,18 +1453,26 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
     return fail(PACE_ERR_TOO_LARGE, "%s: shape too large", name);
   if (max_position <= 0) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: empty cos_sin_cache", name);
   if (num_tokens == 0) return PACE_OK;
-  if (!qkv_out || !hidden || !weight || !positions || !cos_sin_cache || !workspace)
+  // at most kGemvTokens tokens: the CUDA-core kernel, no workspace
+  const bool gemv = num_tokens <= kGemvTokens;
+  if (!qkv_out || !hidden || !weight || !positions || !cos_sin_cache || (!workspace && !gemv))
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
   if (!aligned16(qkv_out) || !aligned16(hidden) || !aligned16(weight) ||
-      !aligned16(cos_sin_cache) || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+      !aligned16(cos_sin_cache) || (!gemv && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0))
     return fail(PACE_ERR_INVALID_ARGUMENT,
                 "%s: pointers must be 16-byte aligned (the workspace 256-byte aligned)", name);
   StreamDeviceGuard guard(stream);
   const int dev = guard.device();
   const QkvShape sh = qkv_shape(num_tokens, hidden_size, heads, sm_count(dev));
-  if (workspace_bytes < sh.workspace_bytes)
+  if (!gemv && workspace_bytes < sh.workspace_bytes)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
                 workspace_bytes, sh.workspace_bytes);
+  const int rot_heads = num_heads + num_kv_heads;
+  if (gemv)
+    return launch_gemv_rope<false>(
+        hidden, hidden_row_stride, weight, hidden_size, qkv_out, out_row_stride, num_tokens,
+        rope_params(positions, cos_sin_cache, max_position, rot_heads, heads), dtype,
+        cache_dtype, is_neox != 0, fault_flags, dev, stream, name);
   const bool bf16 = dtype == PACE_BF16;
   CUtensorMap ma, mb;
   int st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
@@ -1176,7 +1480,6 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
   st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size,
                            sh.pair ? BN / 2 : BN, name);
   if (st != PACE_OK) return st;
-  const int rot_heads = num_heads + num_kv_heads;
 #define PACE_QKV_ROPE(T, C, NX)                                                                 \
   launch_qkv_rope<T, C, NX>(ma, mb, qkv_out, out_row_stride, positions, cos_sin_cache,         \
                             max_position, num_tokens, sh, rot_heads, heads, workspace,         \
@@ -1201,7 +1504,7 @@ namespace {
 // Shape and pointer checks shared by the two entry points below.
 int check_gemm_args(const char* name, int64_t num_tokens, int64_t n, int64_t k, int64_t a_stride,
                     int64_t out_stride, int dtype, const void* out, const void* a, const void* w,
-                    const void* workspace) {
+                    const void* workspace, bool need_workspace = true) {
   if (num_tokens < 0 || num_tokens > ((int64_t)1 << 24) || n <= 0 || k <= 0 ||
       n > (int64_t)INT32_MAX || k > (int64_t)INT32_MAX * BK)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: bad shape", name);
@@ -1214,9 +1517,10 @@ int check_gemm_args(const char* name, int64_t num_tokens, int64_t n, int64_t k, 
     return fail(PACE_ERR_INVALID_ARGUMENT,
                 "%s: K and row strides must be multiples of 8 elements", name);
   if (num_tokens == 0) return PACE_OK;
-  if (!out || !a || !w || !workspace) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!out || !a || !w || (need_workspace && !workspace))
+    return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
   if (!aligned16(out) || !aligned16(a) || !aligned16(w) ||
-      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+      (need_workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0))
     return fail(PACE_ERR_INVALID_ARGUMENT,
                 "%s: pointers must be 16-byte aligned (the workspace 256-byte aligned)", name);
   return PACE_OK;
@@ -1238,12 +1542,12 @@ extern "C" int pace_linear_residual(void* residual, const void* input, const voi
                                     int32_t* fault_flags, cudaStream_t stream) {
   using namespace pace;
   const char* name = "linear_residual";
-  int st = check_gemm_args(name, num_tokens, n, k, input_row_stride, residual_row_stride, dtype,
-                           residual, input, weight, workspace);
-  if (st != PACE_OK || num_tokens == 0) return st;
   if (n % HEAD != 0)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: n = %lld must be a multiple of %d", name,
                 (long long)n, HEAD);
+  int st = check_gemm_args(name, num_tokens, n, k, input_row_stride, residual_row_stride, dtype,
+                           residual, input, weight, workspace);
+  if (st != PACE_OK || num_tokens == 0) return st;
   StreamDeviceGuard guard(stream);
   const int dev = guard.device();
   const QkvShape sh = qkv_shape(num_tokens, k, (int)(n / HEAD), sm_count(dev));
@@ -1293,8 +1597,10 @@ extern "C" int pace_qkv_proj_rmsnorm_rope(
                 (long long)sumsq_groups);
   const int heads = num_heads + 2 * num_kv_heads;
   const int64_t n = (int64_t)heads * head_size;
+  // at most kGemvTokens tokens: the CUDA-core kernel, no workspace
+  const bool gemv = num_tokens <= kGemvTokens;
   int st = check_gemm_args(name, num_tokens, n, hidden_size, hidden_row_stride, out_row_stride,
-                           dtype, qkv_out, hidden, folded_weight, workspace);
+                           dtype, qkv_out, hidden, folded_weight, workspace, !gemv);
   if (st != PACE_OK || num_tokens == 0) return st;
   if (max_position <= 0) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: empty cos_sin_cache", name);
   if (!positions || !cos_sin_cache || !row_sumsq)
@@ -1307,9 +1613,19 @@ extern "C" int pace_qkv_proj_rmsnorm_rope(
   StreamDeviceGuard guard(stream);
   const int dev = guard.device();
   const QkvShape sh = qkv_shape(num_tokens, hidden_size, heads, sm_count(dev));
-  if (workspace_bytes < sh.workspace_bytes)
+  if (!gemv && workspace_bytes < sh.workspace_bytes)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
                 workspace_bytes, sh.workspace_bytes);
+  EpiParams ep = rope_params(positions, cos_sin_cache, max_position, num_heads + num_kv_heads,
+                             heads);
+  ep.sumsq_in = row_sumsq;
+  ep.sumsq_in_groups = (int)sumsq_groups;
+  ep.inv_k = 1.f / (float)hidden_size;
+  ep.eps = epsilon;
+  if (gemv)
+    return launch_gemv_rope<true>(hidden, hidden_row_stride, folded_weight, hidden_size, qkv_out,
+                                  out_row_stride, num_tokens, ep, dtype, cache_dtype,
+                                  is_neox != 0, fault_flags, dev, stream, name);
   const bool bf16 = dtype == PACE_BF16;
   CUtensorMap ma, mb;
   st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM, name);
@@ -1317,12 +1633,6 @@ extern "C" int pace_qkv_proj_rmsnorm_rope(
   st = tc::make_kmajor_map(&mb, folded_weight, bf16, n, hidden_size, hidden_size,
                            sh.pair ? BN / 2 : BN, name);
   if (st != PACE_OK) return st;
-  EpiParams ep = rope_params(positions, cos_sin_cache, max_position, num_heads + num_kv_heads,
-                             heads);
-  ep.sumsq_in = row_sumsq;
-  ep.sumsq_in_groups = (int)sumsq_groups;
-  ep.inv_k = 1.f / (float)hidden_size;
-  ep.eps = epsilon;
 #define PACE_QKV_NORM(T, C, E)                                                                  \
   launch_gemm_epi<T, C, E, true>(ma, mb, qkv_out, out_row_stride, num_tokens, sh, ep, workspace, \
                                  fault_flags, dev, stream, name)
@@ -1509,6 +1819,12 @@ extern "C" int pace_qkv_proj_rope_no_alloc(
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: pointers must be 16-byte aligned", name);
   StreamDeviceGuard guard(stream);
   const int dev = guard.device();
+  const int rot_heads = num_heads + num_kv_heads;
+  if (num_tokens <= kGemvTokens)  // no scratch needed
+    return launch_gemv_rope<false>(
+        hidden, hidden_row_stride, weight, hidden_size, qkv_out, out_row_stride, num_tokens,
+        rope_params(positions, cos_sin_cache, max_position, rot_heads, heads), dtype,
+        cache_dtype, is_neox != 0, fault_flags, dev, stream, name);
   void* scratch = no_alloc_scratch(dev);
   if (!scratch) return PACE_ERR_CUDA;
   QkvShape sh = qkv_shape(num_tokens, hidden_size, heads, sm_count(dev));
@@ -1529,7 +1845,6 @@ extern "C" int pace_qkv_proj_rope_no_alloc(
   st = tc::make_kmajor_map(&mb, weight, bf16, n, hidden_size, hidden_size,
                            sh.pair ? BN / 2 : BN, name);
   if (st != PACE_OK) return st;
-  const int rot_heads = num_heads + num_kv_heads;
 #define PACE_QKV_ROPE_NA(T, C, NX)                                                               \
   launch_qkv_rope<T, C, NX>(ma, mb, qkv_out, out_row_stride, positions, cos_sin_cache,         \
                             max_position, num_tokens, sh, rot_heads, heads, scratch,           \

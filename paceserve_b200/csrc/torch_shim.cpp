@@ -199,6 +199,10 @@ Tensor qkv_workspace(const at::Device& dev, cudaStream_t stream, size_t bytes) {
   return ws;
 }
 
+// A workspace tensor as the C ABI takes it (an undefined tensor: none).
+void* ws_ptr(const Tensor& ws) { return ws.defined() ? ws.data_ptr() : nullptr; }
+size_t ws_bytes(const Tensor& ws) { return ws.defined() ? (size_t)ws.nbytes() : 0; }
+
 void qkv_proj_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& weight, Tensor& positions,
                                int64_t head_size, int64_t num_heads, int64_t num_kv_heads,
                                Tensor& cos_sin_cache, bool is_neox,
@@ -245,7 +249,7 @@ void qkv_proj_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& weight, Tens
                     (size_t)ws.nbytes() >= need,
                 op, ": workspace must be a contiguous tensor of at least ", need, " bytes on ",
                 hidden.device());
-  } else {
+  } else if (need > 0) {  // none at decode sizes
     ws = qkv_workspace(hidden.device(), stream, need);
   }
   check_status(pace_qkv_proj_rope(qkv.data_ptr(), hidden.data_ptr(), weight.data_ptr(),
@@ -253,8 +257,8 @@ void qkv_proj_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& weight, Tens
                                   (int)num_kv_heads, (int)head_size, h.stride, o.stride,
                                   cos_sin_cache.data_ptr(), pace_dtype(cos_sin_cache),
                                   (int)cos_sin_cache.size(1), cos_sin_cache.size(0),
-                                  is_neox ? 1 : 0, pace_dtype(hidden), ws.data_ptr(),
-                                  (size_t)ws.nbytes(), fault, stream),
+                                  is_neox ? 1 : 0, pace_dtype(hidden), ws_ptr(ws),
+                                  ws_bytes(ws), fault, stream),
                op);
 }
 
@@ -269,8 +273,10 @@ Tensor gemm_workspace(const c10::optional<Tensor>& workspace, const at::Device& 
                 dev);
     return ws;
   }
+  if (need == 0) return Tensor();  // the call needs none
   return qkv_workspace(dev, stream, need);
 }
+
 
 // residual <- residual + input @ weight^T (o_proj / down_proj with the residual
 // add in the epilogue); row_sumsq (optional, float32 [T, n / 32]) receives the
@@ -314,7 +320,7 @@ void linear_residual(Tensor& residual, Tensor& input, Tensor& weight,
   int32_t* fault = counter_ptr(fault_flags, input.device(), op, "fault_flags");
   check_status(pace_linear_residual(residual.data_ptr(), input.data_ptr(), weight.data_ptr(), ss,
                                     a.rows, r.width, a.width, a.stride, r.stride,
-                                    pace_dtype(input), ws.data_ptr(), (size_t)ws.nbytes(), fault,
+                                    pace_dtype(input), ws_ptr(ws), ws_bytes(ws), fault,
                                     stream),
                op);
 }
@@ -380,7 +386,7 @@ void qkv_proj_rmsnorm_rotary_embedding(Tensor& qkv, Tensor& hidden, Tensor& fold
                    (int)num_kv_heads, (int)head_size, h.stride, o.stride,
                    cos_sin_cache.data_ptr(), pace_dtype(cos_sin_cache),
                    (int)cos_sin_cache.size(1), cos_sin_cache.size(0), is_neox ? 1 : 0,
-                   pace_dtype(hidden), ws.data_ptr(), (size_t)ws.nbytes(), fault, stream),
+                   pace_dtype(hidden), ws_ptr(ws), ws_bytes(ws), fault, stream),
                op);
 }
 
@@ -427,7 +433,7 @@ void gate_up_silu(Tensor& out, Tensor& hidden, Tensor& weight,
   int32_t* fault = counter_ptr(fault_flags, hidden.device(), op, "fault_flags");
   check_status(pace_gate_up_silu(out.data_ptr(), hidden.data_ptr(), weight.data_ptr(), ss,
                                  h.width / 32, (float)epsilon, h.rows, h.width, o.width, h.stride,
-                                 o.stride, pace_dtype(hidden), ws.data_ptr(), (size_t)ws.nbytes(),
+                                 o.stride, pace_dtype(hidden), ws_ptr(ws), ws_bytes(ws),
                                  fault, stream),
                op);
 }

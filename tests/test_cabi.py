@@ -69,6 +69,11 @@ def test_argument_errors_need_no_gpu():
             cabi.PACE_ERR_INVALID_ARGUMENT, "rot_dim")
     _expect(lib.pace_silu_and_mul(None, None, 4, 8, 8, 8, cabi.PACE_BF16, None),
             cabi.PACE_ERR_INVALID_ARGUMENT, "row stride")
+    # the qkv projection needs no workspace up to 2 tokens (CUDA-core kernel),
+    # the stream-K workspace from 3 on; 0 also for a bad shape
+    assert lib.pace_qkv_proj_rope_workspace_size(2, 4096, 32, 8, 0) == 0
+    assert lib.pace_qkv_proj_rope_workspace_size(3, 4096, 32, 8, 0) > 0
+    assert lib.pace_qkv_proj_rope_workspace_size(3, 4096, 0, 0, 0) == 0
     tab = cabi.layer_table([0])
     _expect(lib.pace_kv_copy_blocks(tab, tab, 0, None, None, 1, 65536, 1, 1, None, 0, None),
             cabi.PACE_ERR_INVALID_ARGUMENT, "num_layers")

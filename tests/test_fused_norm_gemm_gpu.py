@@ -78,7 +78,7 @@ def test_linear_residual_float16_strided_rows_without_sumsq(T):
     assert torch.equal(res_wide[:, N:], tail)  # nothing written past the row
 
 
-@pytest.mark.parametrize("T", [1, 64, 256, 512])
+@pytest.mark.parametrize("T", [1, 2, 3, 64, 256, 512])
 @pytest.mark.parametrize("neox", [True, False])
 def test_qkv_proj_rmsnorm_rope(T, neox):
     nq, nkv, hd, H = 32, 8, 128, 4096

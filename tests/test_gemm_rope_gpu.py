@@ -53,10 +53,11 @@ def check(got, ref, dtype, tight=True):
         assert ((g - r).abs() <= bound).all(), ((g - r).abs() - bound).max().item()
 
 
-@pytest.mark.parametrize("T", [1, 17, 128, 200, 256, 300, 512])
+@pytest.mark.parametrize("T", [1, 2, 3, 17, 128, 200, 256, 300, 512])
 @pytest.mark.parametrize("neox", [True, False])
 def test_llama3_8b_shape(T, neox):
-    # T <= 128: single CTAs (T = 1 and 17 finish shared tiles by their last
+    # T <= 2: the weight-streaming kernel on CUDA cores; 3 <= T <= 128: single
+    # CTAs on tensor cores (T = 3 and 17 finish shared tiles by their last
     # contributor); T = 200 and 256: CTA pairs, stream-K; 300 and 512: CTA
     # pairs, one data-parallel round
     nq, nkv, hd, H = 32, 8, 128, 4096
@@ -121,6 +122,53 @@ def test_strided_rows_and_out_of_range_positions():
     check(qkv.cpu()[bad], plain[bad], torch.bfloat16)
     # the padding columns past the output row are untouched
     assert (out_big[:, n:].cpu() == 7.0).all()
+
+
+@pytest.mark.parametrize("T,H,dtype,cache_16bit,neox",
+                         [(1, 200, torch.float16, True, True), (2, 4104, torch.bfloat16, False, False),
+                          (1, 1032, torch.float16, False, False), (2, 64, torch.bfloat16, True, True)])
+def test_decode_rows_on_cuda_cores(T, H, dtype, cache_16bit, neox):
+    """At most 2 rows: one warp per rotation pair streams the weight.  K that
+    is not a multiple of the 256 elements a warp reads per pass (H = 200: 25
+    vectors, fewer than the lanes), odd head counts, strided rows, positions
+    out of range, 16-bit caches, and nothing written past the output rows."""
+    nq, nkv, hd = 3, 1, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, dtype, T * 1000 + H)
+    positions[0] = -1  # not rotated
+    if cache_16bit:
+        cache = cache.to(dtype)
+    big = torch.zeros(T, H + 40, dtype=dtype)
+    big[:, 8:8 + H] = hidden
+    n = (nq + 2 * nkv) * hd
+    out_big = torch.full((T, n + 64), 5.0, dtype=dtype, device=DEV)
+    qkv = out_big[:, :n]
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, big.to(DEV)[:, 8:8 + H], weight.to(DEV),
+                                               positions.to(DEV), hd, nq, nkv, cache.to(DEV),
+                                               neox)
+    torch.cuda.synchronize()
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache.float(), neox), dtype)
+    plain = hidden.float() @ weight.float().t()
+    check(qkv.cpu()[:1], plain[:1], dtype)
+    assert (out_big[:, n:].cpu() == 5.0).all()
+
+
+def test_decode_rows_graph_replay_is_deterministic():
+    T, H, nq, nkv, hd = 2, 4096, 32, 8, 128
+    hidden, weight, positions, cache = make_case(T, H, nq, nkv, torch.bfloat16, 31)
+    hd_, wd, pd, cd = hidden.to(DEV), weight.to(DEV), positions.to(DEV), cache.to(DEV)
+    qkv = torch.empty(T, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, device=DEV)
+    pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hd_, wd, pd, hd, nq, nkv, cd, True)
+    torch.cuda.synchronize()
+    first = qkv.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        pos_encoding_ops.qkv_proj_rotary_embedding(qkv, hd_, wd, pd, hd, nq, nkv, cd, True)
+    qkv.zero_()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(qkv, first)
+    check(qkv, reference(hidden, weight, positions, nq, nkv, hd, cache, True), torch.bfloat16)
 
 
 def test_matches_unfused_projection_then_rope():

@@ -35,7 +35,7 @@ def close(got, ref, dtype):
     assert ((g - r).abs() <= bound).all()
 
 
-@pytest.mark.parametrize("T", [512, 37])
+@pytest.mark.parametrize("T", [512, 37, 2])
 def test_no_alloc_matches_the_workspace_entry_point(T):
     lib = cabi.load()
     nq, nkv, hd, H = 32, 8, 128, 4096
