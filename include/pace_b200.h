@@ -185,7 +185,10 @@ int pace_qkv_proj_rmsnorm_rope(void* qkv_out, const void* hidden, const void* fo
  * written: gate and up stay in fp32 through the activation, where the
  * reference rounds them to T first.  intermediate_size a multiple of 128;
  * workspace as pace_qkv_proj_rope (zero-filled, left zeroed, size from
- * pace_gate_up_silu_workspace_size).  Replaces gate_up_proj + silu_and_mul
+ * pace_gate_up_silu_workspace_size).  Up to 2 tokens it runs on the CUDA
+ * cores (gate row i and up row I + i streamed together by one warp) with no
+ * workspace: the size function returns 0 and workspace may be NULL.
+ * Replaces gate_up_proj + silu_and_mul
  * (llama.py:102-104).  No reference kernel. */
 size_t pace_gate_up_silu_workspace_size(int64_t num_tokens, int64_t hidden_size,
                                         int64_t intermediate_size, int device);

@@ -445,16 +445,21 @@ __device__ __forceinline__ void store_partial(uint32_t taddr, float* slot, int h
   }
 }
 
-// SiLU-and-mul of 16 gate values a and 16 up values b (NORM: both scaled by the
-// row's factor first), into a.
+// SiLU-and-mul of gate value g and up value u (NORM: both scaled by the row's
+// factor first).
+template <bool NORM>
+__device__ __forceinline__ float silu_mul(float g, float u, float inv) {
+  if (NORM) {
+    g *= inv;
+    u *= inv;
+  }
+  return g / (1.f + __expf(-g)) * u;
+}
+// The same for 16 gate values a and 16 up values b, into a.
 template <bool NORM>
 __device__ __forceinline__ void silu_mul16(float* a, const float* b, float inv) {
 #pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    const float g = NORM ? a[e] * inv : a[e];
-    const float u = NORM ? b[e] * inv : b[e];
-    a[e] = g / (1.f + __expf(-g)) * u;
-  }
+  for (int e = 0; e < 16; ++e) a[e] = silu_mul<NORM>(a[e], b[e], inv);
 }
 
 // A whole gate/up tile from TMEM: this thread's row, output columns
@@ -970,13 +975,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ------------------------------------------ decode batches on CUDA cores --
-// With at most kGemvTokens rows the projection is a stream of the weight
-// (50 MB for Llama-3-8B's qkv) past a few hidden rows: HBM-bound, with a
-// 128-row MMA tile almost all padding and the split-K reduction that the tile
-// schedule needs at this size costing more than the stream itself.  A CTA
-// owns up to kGemvPairs rotation pairs of output columns (NeoX: head columns
-// i and i + 64; GPT-J: 2i and 2i + 1) over the whole K, so no sum crosses
-// CTAs; the pairs are spread evenly over three CTAs per SM.  One producer
+// With at most kGemvTokens rows a projection is a stream of its weight (50 MB
+// for Llama-3-8B's qkv, 235 MB for gate/up) past a few hidden rows:
+// HBM-bound, with a 128-row MMA tile almost all padding and the split-K
+// reduction that the tile schedule needs at this size costing more than the
+// stream itself.  The work unit is a pair of weight rows: a rotation pair of
+// output columns (NeoX: head columns i and i + 64; GPT-J: 2i and 2i + 1), or
+// the gate and up rows of one output column (SiLU-and-mul).  A CTA owns up to
+// kGemvPairs units over the whole K, so no sum crosses CTAs; the units are
+// spread evenly over three CTAs per SM (more CTAs, in waves, when there are
+// more than 8 units per CTA).  One producer
 // thread streams the pairs' weight rows through a ring of kGemvStages
 // shared-memory stages with bulk copies (kGemvChunk elements of every row per
 // stage, 64 KB in flight per CTA: register loads could not keep enough bytes
@@ -984,9 +992,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // row chunks to registers, releases the stage, and dots them with the hidden
 // rows (read through L1, which the CTA's warps share); after the last chunk it
 // reduces across the warp, and lane t finishes token t as the tensor-core
-// epilogue does: norm factor, rotation in fp32, one rounding.  Every wait is
-// bounded; on expiry the CTA sets bit 30 of the fault word, stops, and the
-// producer waits (bounded) for its copies before leaving.
+// epilogue does: norm factor, then the rotation or SiLU-and-mul in fp32, one
+// rounding.  Every wait is bounded; on expiry the CTA sets bit 30 of the
+// fault word, stops, and the producer waits (bounded) for its copies before
+// leaving.
 constexpr int kGemvTokens = 2, kGemvPairs = 8, kGemvChunk = 512, kGemvStages = 4;
 constexpr int kGemvStageElems = 2 * kGemvPairs * kGemvChunk;  // 16-bit weights
 constexpr int kGemvThreads = (kGemvPairs + 1) * 32;
@@ -1014,28 +1023,42 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-template <bool NEOX>
-__device__ __forceinline__ void pair_columns(int unit, int& head, int& i, int& c1, int& c2) {
+// The two weight rows of work unit `unit`: a rotation pair of output columns
+// (rope; head and i locate the pair's cache entry), or gate row `unit` and up
+// row n_cols + unit of output column `unit` (SiLU-and-mul).
+template <int EPI>
+__device__ __forceinline__ void pair_columns(int unit, int n_cols, int& head, int& i, int& c1,
+                                             int& c2) {
+  if (EPI == EPI_GATEUP_SILU) {
+    head = i = 0;
+    c1 = unit;
+    c2 = n_cols + unit;
+    return;
+  }
   head = unit / (HEAD / 2);
   i = unit % (HEAD / 2);
-  c1 = head * HEAD + (NEOX ? i : 2 * i);
-  c2 = c1 + (NEOX ? HEAD / 2 : 1);
+  c1 = head * HEAD + (EPI == EPI_ROPE_NEOX ? i : 2 * i);
+  c2 = c1 + (EPI == EPI_ROPE_NEOX ? HEAD / 2 : 1);
+}
+template <int EPI>
+__host__ __device__ __forceinline__ int gemv_units(int n_cols) {
+  return EPI == EPI_GATEUP_SILU ? n_cols : n_cols / 2;
 }
 
 // NT: tokens the loops are unrolled for (num_tokens <= NT).  Measured on
 // B200 (Llama-3-8B qkv, 50 MB of weight): 9.8 us at one token, 12.9 at two,
 // against 11.9 for cuBLAS's GEMM alone; from three tokens on the tensor-core
 // kernel is faster, so kGemvTokens is 2.
-template <typename T, typename C, bool NEOX, bool NORM, int NT>
+template <typename T, typename C, int EPI, bool NORM, int NT>
 __global__ void __launch_bounds__(kGemvThreads, 3)
-    gemv_rope_kernel(const T* __restrict__ hidden, int64_t hidden_stride,
+    gemv_epi_kernel(const T* __restrict__ hidden, int64_t hidden_stride,
                      const T* __restrict__ weight, int64_t k, T* __restrict__ out,
                      int64_t out_stride, int num_tokens, const EpiParams ep, int32_t* fault) {
   extern __shared__ __align__(16) uint8_t gemv_smem[];
   T* ring = reinterpret_cast<T*>(gemv_smem);
   GemvCtl* ctl = reinterpret_cast<GemvCtl*>(gemv_smem + kGemvStages * kGemvStageElems * 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int units = ep.n_cols / 2;
+  const int units = gemv_units<EPI>(ep.n_cols);
   const int unit0 = (int)((int64_t)blockIdx.x * units / gridDim.x);
   const int pairs = (int)((int64_t)(blockIdx.x + 1) * units / gridDim.x) - unit0;
   const int chunks = (int)ceil_div(k, kGemvChunk);
@@ -1069,7 +1092,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
       T* st = ring + (size_t)s * kGemvStageElems;
       for (int j = 0; j < pairs; ++j) {
         int head, i, c1, c2;
-        pair_columns<NEOX>(unit0 + j, head, i, c1, c2);
+        pair_columns<EPI>(unit0 + j, ep.n_cols, head, i, c1, c2);
         bulk_g2s(st + (2 * j) * kGemvChunk, weight + (int64_t)c1 * k + k0, bytes, &ctl->full[s]);
         bulk_g2s(st + (2 * j + 1) * kGemvChunk, weight + (int64_t)c2 * k + k0, bytes,
                  &ctl->full[s]);
@@ -1089,7 +1112,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   // ---- consumer warp `warp`: rotation pair unit0 + warp ------------------
   const bool has = warp < pairs;
   int head = 0, i = 0, c1 = 0, c2 = 0;
-  if (has) pair_columns<NEOX>(unit0 + warp, head, i, c1, c2);
+  if (has) pair_columns<EPI>(unit0 + warp, ep.n_cols, head, i, c1, c2);
   float acc1[NT], acc2[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc1[t] = acc2[t] = 0.f;
@@ -1179,6 +1202,11 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
       inv = f[t];
     }
   }
+  T* o = out + (int64_t)lane * out_stride;
+  if (EPI == EPI_GATEUP_SILU) {
+    o[c1] = Traits<T>::from_f(silu_mul<NORM>(x1, x2, inv));
+    return;
+  }
   if (NORM) {
     x1 *= inv;
     x2 *= inv;
@@ -1191,7 +1219,6 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     x1 = y1;
     x2 = y2;
   }
-  T* o = out + (int64_t)lane * out_stride;
   o[c1] = Traits<T>::from_f(x1);
   o[c2] = Traits<T>::from_f(x2);
 }
@@ -1327,12 +1354,11 @@ EpiParams rope_params(const int64_t* positions, const void* cache, int64_t max_p
 }
 
 // The decode-batch projection (gemv_rope_kernel) for the dtype pair.
-template <typename T, typename C, bool NEOX, bool NORM, int NT>
-cudaError_t launch_gemv_rope_nt(const void* hidden, int64_t hidden_stride, const void* weight,
-                                int64_t k, void* out, int64_t out_stride, int64_t num_tokens,
-                                const EpiParams& ep, int32_t* fault, int dev,
-                                cudaStream_t stream) {
-  auto kernel = gemv_rope_kernel<T, C, NEOX, NORM, NT>;
+template <typename T, typename C, int EPI, bool NORM, int NT>
+cudaError_t launch_gemv_nt(const void* hidden, int64_t hidden_stride, const void* weight,
+                           int64_t k, void* out, int64_t out_stride, int64_t num_tokens,
+                           const EpiParams& ep, int32_t* fault, int dev, cudaStream_t stream) {
+  auto kernel = gemv_epi_kernel<T, C, EPI, NORM, NT>;
   cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), dev, kGemvSmem);
   if (err != cudaSuccess) return err;
   // three CTAs per SM, so the whole grid is resident at once (set once per
@@ -1344,8 +1370,8 @@ cudaError_t launch_gemv_rope_nt(const void* hidden, int64_t hidden_stride, const
     if (err != cudaSuccess) return err;
     carveout_set[dev].store(true, std::memory_order_release);
   }
-  // the pairs spread over three CTAs per SM, at most kGemvPairs per CTA
-  const int64_t units = ep.n_cols / 2;
+  // the units spread over three CTAs per SM, at most kGemvPairs per CTA
+  const int64_t units = gemv_units<EPI>(ep.n_cols);
   const int64_t grid =
       std::max<int64_t>(ceil_div(units, kGemvPairs), std::min<int64_t>(units, 3 * sm_count(dev)));
   return launch(kernel, dim3((unsigned)grid), dim3(kGemvThreads), kGemvSmem, stream,
@@ -1353,26 +1379,27 @@ cudaError_t launch_gemv_rope_nt(const void* hidden, int64_t hidden_stride, const
                 static_cast<T*>(out), out_stride, (int)num_tokens, ep, fault);
 }
 
-template <typename T, typename C, bool NEOX, bool NORM>
-cudaError_t launch_gemv_rope_t(const void* hidden, int64_t hidden_stride, const void* weight,
-                               int64_t k, void* out, int64_t out_stride, int64_t num_tokens,
-                               const EpiParams& ep, int32_t* fault, int dev,
-                               cudaStream_t stream) {
+template <typename T, typename C, int EPI, bool NORM>
+cudaError_t launch_gemv_t(const void* hidden, int64_t hidden_stride, const void* weight,
+                          int64_t k, void* out, int64_t out_stride, int64_t num_tokens,
+                          const EpiParams& ep, int32_t* fault, int dev, cudaStream_t stream) {
   if (num_tokens == 1)
-    return launch_gemv_rope_nt<T, C, NEOX, NORM, 1>(hidden, hidden_stride, weight, k, out,
-                                                    out_stride, num_tokens, ep, fault, dev, stream);
-  return launch_gemv_rope_nt<T, C, NEOX, NORM, kGemvTokens>(
-      hidden, hidden_stride, weight, k, out, out_stride, num_tokens, ep, fault, dev, stream);
+    return launch_gemv_nt<T, C, EPI, NORM, 1>(hidden, hidden_stride, weight, k, out, out_stride,
+                                              num_tokens, ep, fault, dev, stream);
+  return launch_gemv_nt<T, C, EPI, NORM, kGemvTokens>(hidden, hidden_stride, weight, k, out,
+                                                      out_stride, num_tokens, ep, fault, dev,
+                                                      stream);
 }
 
+// The decode-batch qkv projection for the dtype pair.
 template <bool NORM>
 int launch_gemv_rope(const void* hidden, int64_t hidden_stride, const void* weight, int64_t k,
                      void* out, int64_t out_stride, int64_t num_tokens, const EpiParams& ep,
                      int dtype, int cache_dtype, bool neox, int32_t* fault, int dev,
                      cudaStream_t stream, const char* name) {
 #define PACE_GEMV(T, C, NX)                                                                      \
-  launch_gemv_rope_t<T, C, NX, NORM>(hidden, hidden_stride, weight, k, out, out_stride,          \
-                                     num_tokens, ep, fault, dev, stream)
+  launch_gemv_t<T, C, NX ? EPI_ROPE_NEOX : EPI_ROPE_GPTJ, NORM>(                                 \
+      hidden, hidden_stride, weight, k, out, out_stride, num_tokens, ep, fault, dev, stream)
   cudaError_t err;
   const bool f32c = cache_dtype == PACE_F32;
   if (dtype == PACE_BF16) {
@@ -1666,6 +1693,7 @@ extern "C" size_t pace_gate_up_silu_workspace_size(int64_t num_tokens, int64_t h
   if (num_tokens <= 0 || hidden_size <= 0 || intermediate_size <= 0 ||
       intermediate_size % HEAD != 0 || intermediate_size / HEAD > INT32_MAX / 2)
     return 0;
+  if (num_tokens <= kGemvTokens) return 0;  // the CUDA-core kernel needs none
   // 2 I accumulator columns per row: one 256-column tile per 128 output columns
   return qkv_shape(num_tokens, hidden_size, (int)(2 * intermediate_size / HEAD),
                    sm_count(device))
@@ -1685,8 +1713,10 @@ extern "C" int pace_gate_up_silu(void* out, const void* hidden, const void* weig
       intermediate_size / HEAD > INT32_MAX / 2)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: intermediate size %lld must be a multiple of %d",
                 name, (long long)intermediate_size, HEAD);
+  // at most kGemvTokens tokens: the CUDA-core kernel, no workspace
+  const bool gemv = num_tokens <= kGemvTokens;
   int st = check_gemm_args(name, num_tokens, intermediate_size, hidden_size, hidden_row_stride,
-                           out_row_stride, dtype, out, hidden, weight, workspace);
+                           out_row_stride, dtype, out, hidden, weight, workspace, !gemv);
   if (st != PACE_OK || num_tokens == 0) return st;
   if (row_sumsq) {
     if (sumsq_groups <= 0 || sumsq_groups > hidden_size || sumsq_groups % 4 != 0 ||
@@ -1699,10 +1729,29 @@ extern "C" int pace_gate_up_silu(void* out, const void* hidden, const void* weig
   const int dev = guard.device();
   const QkvShape sh =
       qkv_shape(num_tokens, hidden_size, (int)(2 * intermediate_size / HEAD), sm_count(dev));
-  if (workspace_bytes < sh.workspace_bytes)
+  if (!gemv && workspace_bytes < sh.workspace_bytes)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
                 workspace_bytes, sh.workspace_bytes);
+  EpiParams ep = {};
+  ep.n_cols = (int)intermediate_size;
+  ep.sumsq_in = row_sumsq;
+  ep.sumsq_in_groups = (int)sumsq_groups;
+  ep.inv_k = 1.f / (float)hidden_size;
+  ep.eps = epsilon;
   const bool bf16 = dtype == PACE_BF16;
+  if (gemv) {
+#define PACE_GATE_UP_GEMV(T, NORM)                                                              \
+  launch_gemv_t<T, T, EPI_GATEUP_SILU, NORM>(hidden, hidden_row_stride, weight, hidden_size, out, \
+                                             out_row_stride, num_tokens, ep, fault_flags, dev,    \
+                                             stream)
+    const cudaError_t err =
+        bf16 ? (row_sumsq ? PACE_GATE_UP_GEMV(__nv_bfloat16, true)
+                          : PACE_GATE_UP_GEMV(__nv_bfloat16, false))
+             : (row_sumsq ? PACE_GATE_UP_GEMV(__half, true) : PACE_GATE_UP_GEMV(__half, false));
+#undef PACE_GATE_UP_GEMV
+    if (err != cudaSuccess) return cuda_fail(err, name);
+    return PACE_OK;
+  }
   CUtensorMap ma, mb;
   st = tc::make_kmajor_map(&ma, hidden, bf16, num_tokens, hidden_size, hidden_row_stride, BM,
                            name);
@@ -1711,12 +1760,6 @@ extern "C" int pace_gate_up_silu(void* out, const void* hidden, const void* weig
   st = tc::make_kmajor_map(&mb, weight, bf16, 2 * intermediate_size, hidden_size, hidden_size,
                            HEAD, name);
   if (st != PACE_OK) return st;
-  EpiParams ep = {};
-  ep.n_cols = (int)intermediate_size;
-  ep.sumsq_in = row_sumsq;
-  ep.sumsq_in_groups = (int)sumsq_groups;
-  ep.inv_k = 1.f / (float)hidden_size;
-  ep.eps = epsilon;
 #define PACE_GATE_UP(T, NORM)                                                                   \
   launch_gemm_epi<T, float, EPI_GATEUP_SILU, NORM>(ma, mb, out, out_row_stride, num_tokens, sh, \
                                                    ep, workspace, fault_flags, dev, stream, name)

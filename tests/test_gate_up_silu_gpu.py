@@ -45,9 +45,12 @@ def ref_gate_up(x32, w, inter):
     return gate * torch.sigmoid(gate) * up
 
 
-@pytest.mark.parametrize("T,H,I", [(1, 4096, 14336), (37, 1024, 512), (200, 1024, 384),
-                                   (512, 4096, 14336), (1000, 2048, 1024)])
+@pytest.mark.parametrize("T,H,I", [(1, 4096, 14336), (2, 200, 384), (3, 1024, 256),
+                                   (37, 1024, 512), (200, 1024, 384), (512, 4096, 14336),
+                                   (1000, 2048, 1024)])
 def test_gate_up_silu(T, H, I):
+    # T <= 2: the weight-streaming kernel on CUDA cores (H = 200: fewer 16-byte
+    # vectors per row than lanes); from T = 3 the tensor-core GEMM
     g = torch.Generator().manual_seed(T + H + I)
     x = rnd((T, H), g).to(DEV)
     w = rnd((2 * I, H), g, H ** -0.5).to(DEV)
@@ -75,8 +78,9 @@ def test_gate_up_silu_fewer_leftover_units_than_ctas():
         close(out, ref, torch.bfloat16)
 
 
-def test_gate_up_silu_float16_and_strided_rows():
-    T, H, I = 130, 1024, 640
+@pytest.mark.parametrize("T", [2, 130])
+def test_gate_up_silu_float16_and_strided_rows(T):
+    H, I = 1024, 640
     g = torch.Generator().manual_seed(5)
     wide = rnd((T, H + 64), g, dtype=torch.float16).to(DEV)
     x = wide[:, 32:32 + H]  # row stride H + 64, 64-byte offset
@@ -89,7 +93,7 @@ def test_gate_up_silu_float16_and_strided_rows():
     assert (out_wide[:, I:] == 0).all()  # nothing written past the output columns
 
 
-@pytest.mark.parametrize("T", [1, 96, 512])
+@pytest.mark.parametrize("T", [1, 2, 96, 512])
 def test_gate_up_rmsnorm_silu(T):
     H, I = 4096, 14336
     g = torch.Generator().manual_seed(T * 7)
