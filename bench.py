@@ -1150,6 +1150,24 @@ def moe_routing(dev, reps=50):
     return out
 
 
+def gemm_workspace(dev, t):
+    """One zeroed workspace for every fused GEMM of a Llama-3-8B layer at t
+    tokens (stream-ordered calls may share it), or None when none needs one.
+    Passed explicitly, so no CUDA-graph capture records the shim allocating and
+    zero-filling its own."""
+    import torch
+
+    from paceserve_b200 import cabi
+
+    lib = cabi.load()
+    d = torch.device(dev).index or 0
+    need = max(lib.pace_qkv_proj_rope_workspace_size(t, H, NQ, NKV, d),
+               lib.pace_linear_residual_workspace_size(t, H, H, d),
+               lib.pace_linear_residual_workspace_size(t, H, I, d),
+               lib.pace_gate_up_silu_workspace_size(t, H, I, d))
+    return torch.zeros(need, dtype=torch.uint8, device=dev) if need else None
+
+
 def qkv_rope_bench(dev, tokens=(1, 2, 128, 512, 2048), reps=10):
     """The fused qkv projection + rotary embedding (tcgen05 GEMM, rope in the
     epilogue; at most 2 tokens, the weight-streaming CUDA-core kernel) against
@@ -1177,11 +1195,7 @@ def qkv_rope_bench(dev, tokens=(1, 2, 128, 512, 2048), reps=10):
         pos = torch.randint(0, MAX_POS, (t,), generator=g_, device=dev)
         outs = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
         refs = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
-        # the caller's zeroed workspace (none needed at decode sizes), so no
-        # capture records the shim allocating and zero-filling its own
-        need = pb.pos_encoding_ops.qkv_proj_rope_workspace_size(t, H, nq, nkv,
-                                                                torch.device(dev).index or 0)
-        ws = torch.zeros(need, dtype=torch.uint8, device=dev) if need else None
+        ws = gemm_workspace(dev, t)
 
         def fused():
             for x, w, o in zip(xs, weights, outs):
@@ -1259,11 +1273,14 @@ def norm_gemm_bench(dev, tokens=(512, 2048), reps=10):
         qkv_u = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
         xo = [torch.empty(t, H, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
 
+        ws = gemm_workspace(dev, t)
+
         def fused():
             for i in range(nbuf):
-                pb.layernorm_ops.linear_residual(res_f[i], attn[i], w_o[i], ss[i])
+                pb.layernorm_ops.linear_residual(res_f[i], attn[i], w_o[i], ss[i], workspace=ws)
                 pb.pos_encoding_ops.qkv_proj_rmsnorm_rotary_embedding(
-                    qkv_f[i], res_f[i], folded[i], ss[i], EPS, pos, HD, NQ, NKV, cache, True)
+                    qkv_f[i], res_f[i], folded[i], ss[i], EPS, pos, HD, NQ, NKV, cache, True,
+                    workspace=ws)
 
         def unfused():
             for i in range(nbuf):
@@ -1277,7 +1294,7 @@ def norm_gemm_bench(dev, tokens=(512, 2048), reps=10):
 
         res = {"T": t}
         for name, fn, resets in (("fused_us", fused, res_f), ("unfused_us", unfused, res_u)):
-            fn()  # eager once (workspace allocation outside capture)
+            fn()  # eager once
             gr = capture(fn)
             res[name] = round(time_replays(gr, reps, 3) * 1e3 / (reps * nbuf), 3)
             del gr
@@ -1295,7 +1312,7 @@ def norm_gemm_bench(dev, tokens=(512, 2048), reps=10):
     return rows
 
 
-def layer_gemms_bench(dev, tokens=(512, 2048, 8192), reps=5):
+def layer_gemms_bench(dev, tokens=(1, 512, 2048, 8192), reps=5):
     """Everything in a Llama-3-8B decoder layer but attention, bf16: o_proj ->
     residual add -> post-attention RMSNorm -> gate_up_proj -> SiLU-and-mul ->
     down_proj -> residual add -> next input RMSNorm -> qkv_proj -> rope.
@@ -1343,14 +1360,18 @@ def layer_gemms_bench(dev, tokens=(512, 2048, 8192), reps=5):
         xh = [torch.empty(t, H, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
         qkv_f = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
         qkv_u = [torch.empty(t, n, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+        ws = gemm_workspace(dev, t)
 
         def fused():
             for i, s_ in enumerate(sets):
-                pb.layernorm_ops.linear_residual(res_f[i], attn[i], s_["o"], ss1[i])
-                pb.activation_ops.gate_up_silu(act[i], res_f[i], s_["gu_f"], ss1[i], EPS)
-                pb.layernorm_ops.linear_residual(res_f[i], act[i], s_["down"], ss2[i])
+                pb.layernorm_ops.linear_residual(res_f[i], attn[i], s_["o"], ss1[i], workspace=ws)
+                pb.activation_ops.gate_up_silu(act[i], res_f[i], s_["gu_f"], ss1[i], EPS,
+                                               workspace=ws)
+                pb.layernorm_ops.linear_residual(res_f[i], act[i], s_["down"], ss2[i],
+                                                 workspace=ws)
                 pb.pos_encoding_ops.qkv_proj_rmsnorm_rotary_embedding(
-                    qkv_f[i], res_f[i], s_["qkv_f"], ss2[i], EPS, pos, HD, NQ, NKV, cache, True)
+                    qkv_f[i], res_f[i], s_["qkv_f"], ss2[i], EPS, pos, HD, NQ, NKV, cache, True,
+                    workspace=ws)
 
         def unfused():
             for i, s_ in enumerate(sets):
@@ -1368,7 +1389,7 @@ def layer_gemms_bench(dev, tokens=(512, 2048, 8192), reps=5):
 
         res = {"T": t}
         for name, fn, resets in (("fused_us", fused, res_f), ("unfused_us", unfused, res_u)):
-            fn()  # eager once (workspace allocation outside capture)
+            fn()  # eager once
             gr = capture(fn)
             res[name] = round(time_replays(gr, reps, 3) * 1e3 / (reps * nbuf), 3)
             del gr
@@ -1758,8 +1779,10 @@ def main():
         torch.cuda.empty_cache()
         line["layer_gemms"] = {"what": "a Llama-3-8B layer minus attention (o_proj, residual, "
                                        "RMSNorm, gate_up, SiLU-and-mul, down, residual, RMSNorm, "
-                                       "qkv, rope; bf16) as four tensor-core GEMMs with the rest "
-                                       "in their epilogues, vs cuBLAS + this package's ops",
+                                       "qkv, rope; bf16) as four GEMMs with the rest in their "
+                                       "epilogues (tensor cores; at one token the CUDA-core "
+                                       "weight stream, plus row_sumsq twice), vs cuBLAS + this "
+                                       "package's ops",
                                "peak_tflops": pk["bf16_tflops"], "rows": layer_gemms_bench(dev)}
         torch.cuda.empty_cache()
         line["moe_experts"] = {"what": "Mixtral-8x7B expert layer (E=8, top-2, 4096 -> 14336 -> "

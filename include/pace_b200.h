@@ -98,7 +98,8 @@ int pace_rotary_embedding(const int64_t* positions, void* query, void* key, int6
  * rot_dim = 128; hidden_size and both row strides multiples of 8 elements;
  * qkv_out, hidden, weight and the cache 16-byte aligned.  Tokens whose
  * position lies outside [0, max_position) are stored unrotated.
- * Up to 2 tokens (decode batches) the projection runs on the CUDA cores
+ * For one token, or two with hidden_size <= 8192 (decode batches), the
+ * projection runs on the CUDA cores
  * instead: a stream of the weight through shared memory, one warp per
  * rotation pair of output columns over the whole K, the same epilogue; it
  * needs no workspace (pace_qkv_proj_rope_workspace_size returns 0, and
@@ -142,7 +143,10 @@ int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
  *   row_sumsq[t, g] = sum of the new residual's squares over columns
  *   [32g, 32g + 32) (fp32, [T, n / 32]).  Workspace as for
  *   pace_qkv_proj_rope (pace_linear_residual_workspace_size; zero-filled
- *   before first use, left valid by every call).
+ *   before first use, left valid by every call).  For one token, or two with
+ *   k <= 8192, it runs on the CUDA cores with no workspace (size 0, workspace
+ *   may be NULL), and the partials come from pace_row_sumsq on the new rows,
+ *   launched after it.
  * pace_row_sumsq: the same partials for rows no GEMM produced (layer 0).
  * pace_qkv_proj_rmsnorm_rope: pace_qkv_proj_rope on un-normalised rows
  *   `hidden`, with the RMSNorm applied as a per-row factor in the epilogue:
@@ -152,7 +156,7 @@ int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void* weight,
  *   the caller.  Equal to rms_norm then the projection up to the rounding of
  *   the normalised rows (the reference rounds them to T before its GEMM).
  *   row_sumsq 16-byte aligned, sumsq_groups (= hidden_size / 32) a multiple
- *   of 4.  Up to 2 tokens it runs on the CUDA cores without a workspace, as
+ *   of 4.  At decode sizes it runs on the CUDA cores without a workspace, as
  *   pace_qkv_proj_rope does.
  * Replace fused_add_rms_norm + qkv_proj (llama.py:176, 240-254) and the
  * residual add after o_proj / the MLP.  No reference kernel. */
@@ -185,9 +189,10 @@ int pace_qkv_proj_rmsnorm_rope(void* qkv_out, const void* hidden, const void* fo
  * written: gate and up stay in fp32 through the activation, where the
  * reference rounds them to T first.  intermediate_size a multiple of 128;
  * workspace as pace_qkv_proj_rope (zero-filled, left zeroed, size from
- * pace_gate_up_silu_workspace_size).  Up to 2 tokens it runs on the CUDA
- * cores (gate row i and up row I + i streamed together by one warp) with no
- * workspace: the size function returns 0 and workspace may be NULL.
+ * pace_gate_up_silu_workspace_size).  For one token, or two with
+ * hidden_size <= 8192, it runs on the CUDA cores (gate row i and up row I + i
+ * streamed together by one warp) with no workspace: the size function
+ * returns 0 and workspace may be NULL.
  * Replaces gate_up_proj + silu_and_mul
  * (llama.py:102-104).  No reference kernel. */
 size_t pace_gate_up_silu_workspace_size(int64_t num_tokens, int64_t hidden_size,

@@ -981,7 +981,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // reduction that the tile schedule needs at this size costing more than the
 // stream itself.  The work unit is a pair of weight rows: a rotation pair of
 // output columns (NeoX: head columns i and i + 64; GPT-J: 2i and 2i + 1), or
-// the gate and up rows of one output column (SiLU-and-mul).  A CTA owns up to
+// the gate and up rows of one output column (SiLU-and-mul), or two adjacent
+// output columns (residual add, for o_proj and down_proj).  A CTA owns up to
 // kGemvPairs units over the whole K, so no sum crosses CTAs; the units are
 // spread evenly over three CTAs per SM (more CTAs, in waves, when there are
 // more than 8 units per CTA).  One producer
@@ -992,8 +993,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // row chunks to registers, releases the stage, and dots them with the hidden
 // rows (read through L1, which the CTA's warps share); after the last chunk it
 // reduces across the warp, and lane t finishes token t as the tensor-core
-// epilogue does: norm factor, then the rotation or SiLU-and-mul in fp32, one
-// rounding.  Every wait is bounded; on expiry the CTA sets bit 30 of the
+// epilogue does: norm factor, then the rotation, SiLU-and-mul or residual
+// add in fp32, one rounding.  Every wait is bounded; on expiry the CTA sets bit 30 of the
 // fault word, stops, and the producer waits (bounded) for its copies before
 // leaving.
 constexpr int kGemvTokens = 2, kGemvPairs = 8, kGemvChunk = 512, kGemvStages = 4;
@@ -1024,15 +1025,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 
 // The two weight rows of work unit `unit`: a rotation pair of output columns
-// (rope; head and i locate the pair's cache entry), or gate row `unit` and up
-// row n_cols + unit of output column `unit` (SiLU-and-mul).
+// (rope; head and i locate the pair's cache entry), gate row `unit` and up
+// row n_cols + unit of output column `unit` (SiLU-and-mul), or output columns
+// 2 unit and 2 unit + 1 (residual).
 template <int EPI>
 __device__ __forceinline__ void pair_columns(int unit, int n_cols, int& head, int& i, int& c1,
                                              int& c2) {
-  if (EPI == EPI_GATEUP_SILU) {
+  if (EPI == EPI_GATEUP_SILU || EPI == EPI_RESIDUAL) {
     head = i = 0;
-    c1 = unit;
-    c2 = n_cols + unit;
+    c1 = EPI == EPI_RESIDUAL ? 2 * unit : unit;
+    c2 = EPI == EPI_RESIDUAL ? c1 + 1 : n_cols + unit;
     return;
   }
   head = unit / (HEAD / 2);
@@ -1207,6 +1209,11 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     o[c1] = Traits<T>::from_f(silu_mul<NORM>(x1, x2, inv));
     return;
   }
+  if (EPI == EPI_RESIDUAL) {  // the row's residual, updated in place
+    o[c1] = Traits<T>::from_f(x1 + Traits<T>::to_f(o[c1]));
+    o[c2] = Traits<T>::from_f(x2 + Traits<T>::to_f(o[c2]));
+    return;
+  }
   if (NORM) {
     x1 *= inv;
     x2 *= inv;
@@ -1354,6 +1361,14 @@ EpiParams rope_params(const int64_t* positions, const void* cache, int64_t max_p
 }
 
 // The decode-batch projection (gemv_rope_kernel) for the dtype pair.
+// Whether a call of num_tokens rows and reduction length k takes the
+// CUDA-core kernel: always for one token; for two, up to k = 8192 (measured on
+// B200: at two tokens and k = 14336, Llama-3-8B's down_proj, the tensor-core
+// kernel is faster).
+inline bool gemv_path(int64_t num_tokens, int64_t k) {
+  return num_tokens <= 1 || (num_tokens <= kGemvTokens && k <= 8192);
+}
+
 template <typename T, typename C, int EPI, bool NORM, int NT>
 cudaError_t launch_gemv_nt(const void* hidden, int64_t hidden_stride, const void* weight,
                            int64_t k, void* out, int64_t out_stride, int64_t num_tokens,
@@ -1440,7 +1455,7 @@ extern "C" size_t pace_qkv_proj_rope_workspace_size(int64_t num_tokens, int64_t 
   if (num_tokens <= 0 || hidden_size <= 0 || num_heads < 0 || num_kv_heads < 0 ||
       num_heads + num_kv_heads <= 0)
     return 0;
-  if (num_tokens <= kGemvTokens) return 0;  // the CUDA-core kernel needs none
+  if (gemv_path(num_tokens, hidden_size)) return 0;  // the CUDA-core kernel needs none
   return qkv_shape(num_tokens, hidden_size, num_heads + 2 * num_kv_heads, sm_count(device))
       .workspace_bytes;
 }
@@ -1481,7 +1496,7 @@ extern "C" int pace_qkv_proj_rope(void* qkv_out, const void* hidden, const void*
   if (max_position <= 0) return fail(PACE_ERR_INVALID_ARGUMENT, "%s: empty cos_sin_cache", name);
   if (num_tokens == 0) return PACE_OK;
   // at most kGemvTokens tokens: the CUDA-core kernel, no workspace
-  const bool gemv = num_tokens <= kGemvTokens;
+  const bool gemv = gemv_path(num_tokens, hidden_size);
   if (!qkv_out || !hidden || !weight || !positions || !cos_sin_cache || (!workspace && !gemv))
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
   if (!aligned16(qkv_out) || !aligned16(hidden) || !aligned16(weight) ||
@@ -1559,6 +1574,7 @@ extern "C" size_t pace_linear_residual_workspace_size(int64_t num_tokens, int64_
                                                       int device) {
   using namespace pace;
   if (num_tokens <= 0 || n <= 0 || k <= 0 || n % HEAD != 0) return 0;
+  if (gemv_path(num_tokens, k)) return 0;  // the CUDA-core kernel needs none
   return qkv_shape(num_tokens, k, (int)(n / HEAD), sm_count(device)).workspace_bytes;
 }
 
@@ -1572,16 +1588,34 @@ extern "C" int pace_linear_residual(void* residual, const void* input, const voi
   if (n % HEAD != 0)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: n = %lld must be a multiple of %d", name,
                 (long long)n, HEAD);
+  // at most kGemvTokens tokens: the CUDA-core kernel, no workspace
+  const bool gemv = gemv_path(num_tokens, k);
   int st = check_gemm_args(name, num_tokens, n, k, input_row_stride, residual_row_stride, dtype,
-                           residual, input, weight, workspace);
+                           residual, input, weight, workspace, !gemv);
   if (st != PACE_OK || num_tokens == 0) return st;
   StreamDeviceGuard guard(stream);
   const int dev = guard.device();
   const QkvShape sh = qkv_shape(num_tokens, k, (int)(n / HEAD), sm_count(dev));
-  if (workspace_bytes < sh.workspace_bytes)
+  if (!gemv && workspace_bytes < sh.workspace_bytes)
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: workspace of %zu bytes, %zu needed", name,
                 workspace_bytes, sh.workspace_bytes);
   const bool bf16 = dtype == PACE_BF16;
+  if (gemv) {
+    // the new rows, then their sums of squares per 32 columns (the same
+    // partials the tensor-core epilogue writes) by pace_row_sumsq
+    EpiParams ep = {};
+    ep.n_cols = (int)n;
+    const cudaError_t err =
+        bf16 ? launch_gemv_t<__nv_bfloat16, __nv_bfloat16, EPI_RESIDUAL, false>(
+                   input, input_row_stride, weight, k, residual, residual_row_stride, num_tokens,
+                   ep, fault_flags, dev, stream)
+             : launch_gemv_t<__half, __half, EPI_RESIDUAL, false>(
+                   input, input_row_stride, weight, k, residual, residual_row_stride, num_tokens,
+                   ep, fault_flags, dev, stream);
+    if (err != cudaSuccess) return cuda_fail(err, name);
+    if (!row_sumsq) return PACE_OK;
+    return pace_row_sumsq(row_sumsq, residual, num_tokens, n, residual_row_stride, dtype, stream);
+  }
   CUtensorMap ma, mb;
   st = tc::make_kmajor_map(&ma, input, bf16, num_tokens, k, input_row_stride, BM, name);
   if (st != PACE_OK) return st;
@@ -1625,7 +1659,7 @@ extern "C" int pace_qkv_proj_rmsnorm_rope(
   const int heads = num_heads + 2 * num_kv_heads;
   const int64_t n = (int64_t)heads * head_size;
   // at most kGemvTokens tokens: the CUDA-core kernel, no workspace
-  const bool gemv = num_tokens <= kGemvTokens;
+  const bool gemv = gemv_path(num_tokens, hidden_size);
   int st = check_gemm_args(name, num_tokens, n, hidden_size, hidden_row_stride, out_row_stride,
                            dtype, qkv_out, hidden, folded_weight, workspace, !gemv);
   if (st != PACE_OK || num_tokens == 0) return st;
@@ -1693,7 +1727,7 @@ extern "C" size_t pace_gate_up_silu_workspace_size(int64_t num_tokens, int64_t h
   if (num_tokens <= 0 || hidden_size <= 0 || intermediate_size <= 0 ||
       intermediate_size % HEAD != 0 || intermediate_size / HEAD > INT32_MAX / 2)
     return 0;
-  if (num_tokens <= kGemvTokens) return 0;  // the CUDA-core kernel needs none
+  if (gemv_path(num_tokens, hidden_size)) return 0;  // the CUDA-core kernel needs none
   // 2 I accumulator columns per row: one 256-column tile per 128 output columns
   return qkv_shape(num_tokens, hidden_size, (int)(2 * intermediate_size / HEAD),
                    sm_count(device))
@@ -1714,7 +1748,7 @@ extern "C" int pace_gate_up_silu(void* out, const void* hidden, const void* weig
     return fail(PACE_ERR_INVALID_ARGUMENT, "%s: intermediate size %lld must be a multiple of %d",
                 name, (long long)intermediate_size, HEAD);
   // at most kGemvTokens tokens: the CUDA-core kernel, no workspace
-  const bool gemv = num_tokens <= kGemvTokens;
+  const bool gemv = gemv_path(num_tokens, hidden_size);
   int st = check_gemm_args(name, num_tokens, intermediate_size, hidden_size, hidden_row_stride,
                            out_row_stride, dtype, out, hidden, weight, workspace, !gemv);
   if (st != PACE_OK || num_tokens == 0) return st;
@@ -1863,7 +1897,7 @@ extern "C" int pace_qkv_proj_rope_no_alloc(
   StreamDeviceGuard guard(stream);
   const int dev = guard.device();
   const int rot_heads = num_heads + num_kv_heads;
-  if (num_tokens <= kGemvTokens)  // no scratch needed
+  if (gemv_path(num_tokens, hidden_size))  // no scratch needed
     return launch_gemv_rope<false>(
         hidden, hidden_row_stride, weight, hidden_size, qkv_out, out_row_stride, num_tokens,
         rope_params(positions, cos_sin_cache, max_position, rot_heads, heads), dtype,

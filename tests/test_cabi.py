@@ -76,6 +76,11 @@ def test_argument_errors_need_no_gpu():
     assert lib.pace_qkv_proj_rope_workspace_size(3, 4096, 0, 0, 0) == 0
     assert lib.pace_gate_up_silu_workspace_size(2, 4096, 14336, 0) == 0
     assert lib.pace_gate_up_silu_workspace_size(3, 4096, 14336, 0) > 0
+    assert lib.pace_linear_residual_workspace_size(2, 4096, 4096, 0) == 0
+    assert lib.pace_linear_residual_workspace_size(3, 4096, 4096, 0) > 0
+    # two tokens over a long K (down_proj) stay on the tensor cores
+    assert lib.pace_linear_residual_workspace_size(2, 4096, 14336, 0) > 0
+    assert lib.pace_linear_residual_workspace_size(1, 4096, 14336, 0) == 0
     tab = cabi.layer_table([0])
     _expect(lib.pace_kv_copy_blocks(tab, tab, 0, None, None, 1, 65536, 1, 1, None, 0, None),
             cabi.PACE_ERR_INVALID_ARGUMENT, "num_layers")

@@ -34,9 +34,13 @@ def rnd(shape, g, scale=1.0, dtype=torch.bfloat16):
     return (torch.randn(*shape, generator=g) * scale).to(dtype)
 
 
-@pytest.mark.parametrize("T,K,N", [(1, 4096, 4096), (37, 1024, 512), (512, 4096, 4096),
+@pytest.mark.parametrize("T,K,N", [(1, 4096, 4096), (1, 14336, 4096), (2, 200, 256),
+                                   (2, 14336, 4096), (37, 1024, 512), (512, 4096, 4096),
                                    (300, 14336, 4096)])
 def test_linear_residual_and_row_sumsq(T, K, N):
+    # one token, or two with K <= 8192: the weight-streaming CUDA-core kernel,
+    # then row_sumsq on the new rows; otherwise the tensor-core GEMM with the
+    # partials in its epilogue
     g = torch.Generator().manual_seed(T + K)
     a = rnd((T, K), g)
     w = rnd((N, K), g, K ** -0.5)
@@ -58,7 +62,7 @@ def test_linear_residual_and_row_sumsq(T, K, N):
     assert torch.allclose(ss2.cpu().double(), want_ss, rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("T", [20, 300])
+@pytest.mark.parametrize("T", [2, 20, 300])
 def test_linear_residual_float16_strided_rows_without_sumsq(T):
     """fp16 rounding of the residual add; input and residual as column slices
     of wider rows; no sum-of-squares output.  T=20 finishes shared stream-K
