@@ -1360,7 +1360,6 @@ EpiParams rope_params(const int64_t* positions, const void* cache, int64_t max_p
   return ep;
 }
 
-// The decode-batch projection (gemv_rope_kernel) for the dtype pair.
 // Whether a call of num_tokens rows and reduction length k takes the
 // CUDA-core kernel: always for one token; for two, up to k = 8192 (measured on
 // B200: at two tokens and k = 14336, Llama-3-8B's down_proj, the tensor-core
