@@ -1076,7 +1076,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   __syncthreads();
 
   if (warp == kGemvPairs) {
-    // ---- producer: every chunk of every row of the CTA's pairs ----------
+    // ---- producer: every chunk of both rows of the CTA's units -----------
     if (lane != 0) return;
     pdl_wait();
     int c = 0;
@@ -1111,7 +1111,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     return;
   }
 
-  // ---- consumer warp `warp`: rotation pair unit0 + warp ------------------
+  // ---- consumer warp `warp`: unit unit0 + warp ----------------------------
   const bool has = warp < pairs;
   int head = 0, i = 0, c1 = 0, c2 = 0;
   if (has) pair_columns<EPI>(unit0 + warp, ep.n_cols, head, i, c1, c2);
