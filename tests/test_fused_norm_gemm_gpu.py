@@ -2,7 +2,9 @@
 layernorm_ops.linear_residual (o_proj / down_proj with the residual add and the
 next norm's sum-of-squares partials in the epilogue), layernorm_ops.row_sumsq,
 and pos_encoding_ops.qkv_proj_rmsnorm_rotary_embedding (input RMSNorm as a
-per-row factor, qkv projection and rope in one GEMM).
+per-row factor, qkv projection and rope in one GEMM).  At decode sizes the
+same entry points run the weight-streaming CUDA-core kernel (linear_residual
+then computes the partials with row_sumsq).
 
 Oracle: the reference's composition in fp32 from the same 16-bit inputs:
 residual + a @ W^T (models/llama.py:248), then rms_norm (oracle/ops_ref.py),

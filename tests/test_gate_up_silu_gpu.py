@@ -1,5 +1,6 @@
 """GPU parity of activation_ops.gate_up_silu: the MLP's gate_up_proj and
-SiLU-and-mul in one tensor-core GEMM (reference models/llama.py:102-104,
+SiLU-and-mul in one tensor-core GEMM, or at decode sizes one weight stream on
+the CUDA cores (reference models/llama.py:102-104,
 csrc/activation_kernels.cu:15-45), optionally with the post-attention RMSNorm
 applied as a per-row factor (norm weight folded into the GEMM weight).
 

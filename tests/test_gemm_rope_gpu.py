@@ -1,5 +1,6 @@
 """GPU parity of the fused qkv projection + rotary embedding (tcgen05 GEMM with
-the rotation in its epilogue) against the fp32 oracle: the GEMM of the same
+the rotation in its epilogue; at decode sizes the weight-streaming CUDA-core
+kernel with the same epilogue) against the fp32 oracle: the GEMM of the same
 bf16/fp16 inputs in fp32, then the oracle's rotation.  Tolerance: the float
 rule of the per-layer ops, max|got - ref| / max|ref| <= 1e-2, plus a per-element
 bound of a few storage-type ulps (the only differences are the fp32 summation
