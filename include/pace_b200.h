@@ -218,7 +218,9 @@ int pace_gate_up_silu(void* out, const void* hidden, const void* weight, const f
  * calls that may overlap on the GPU (other streams, other host threads) race
  * and must be serialised by the caller.  Each call clears the tile counters
  * it uses on its stream (cudaMemsetAsync) before the kernel; it allocates
- * nothing. */
+ * nothing.  At decode sizes (one token, or two with hidden_size <= 8192) it
+ * runs the same CUDA-core kernel as pace_qkv_proj_rope, which needs no
+ * scratch: no memset, no shared array, no CTA limit. */
 int pace_qkv_proj_rope_no_alloc(void* qkv_out, const void* hidden, const void* weight,
                                 const int64_t* positions, int64_t num_tokens,
                                 int64_t hidden_size, int num_heads, int num_kv_heads,
